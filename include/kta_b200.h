@@ -1,0 +1,130 @@
+/*
+ * libkta_b200 — C ABI of the B200 (sm_100a) kernels behind KTA's kernel cases.
+ *
+ * Every entry is `extern "C"`, takes device pointers as `const void*` / `void*`, sizes as
+ * int64_t and a CUDA stream as `void*` (NULL = the legacy default stream), returns a
+ * kta_status code, and is asynchronous on that stream: no host synchronisation happens
+ * inside. The caller owns every buffer (the library allocates no device memory on any
+ * call path); the library keeps only per-device state: a 64-byte device status block
+ * written by the kernels' watchdogs, and the resolved driver entry point for
+ * cuTensorMapEncodeTiled. Entries are re-entrant across host threads and streams.
+ *
+ * Reference interfaces these entries replace (paths within kernel-template-agent):
+ *   - src/kta/measure/bench.py:94-98 — a `BuiltModule(kind="so")` whose `entry` is called
+ *     through ctypes with the LaunchSpec parameters (device addresses as uint64, shape
+ *     scalars as int32) and launches by itself. The kta_so_* shims below have exactly that
+ *     shape.
+ *   - src/kta/backends/harness/run.py:30-77 and src/kta/targets/cudadrv.py:158-177 — the
+ *     cubin launch of a TileLang kernel; the kta_* entries are their launch-by-itself
+ *     replacements.
+ */
+#ifndef KTA_B200_H
+#define KTA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KTA_ABI_VERSION 1
+
+/* Status codes returned by every entry (and recorded by device watchdogs). */
+enum kta_status_code {
+  KTA_OK = 0,
+  KTA_ERR_INVALID_ARG = 1,    /* null pointer, negative or zero size, bad scale */
+  KTA_ERR_UNSUPPORTED = 2,    /* shape or head_dim outside what the kernel handles */
+  KTA_ERR_ALIGN = 3,          /* pointer or row stride breaks the 16-byte TMA rule */
+  KTA_ERR_LAUNCH = 4,         /* the CUDA launch itself failed */
+  KTA_ERR_DEVICE_TIMEOUT = 5, /* a device-side bounded wait expired (see kta_device_status) */
+  KTA_ERR_NO_DEVICE = 6,      /* no CUDA device or an sm below 10.0 */
+  KTA_ERR_WORKSPACE = 7,      /* workspace missing or smaller than kta_*_workspace_bytes */
+  KTA_ERR_CUDA = 8,           /* another CUDA runtime/driver error */
+  KTA_ERR_DEVICE_BOUNDS = 9   /* a kernel's own bounds check rejected a device-side value */
+};
+
+/* Version of this ABI (KTA_ABI_VERSION of the build). */
+int kta_abi_version(void);
+
+/* Static text of a status code. */
+const char* kta_status_string(int status);
+
+/* Reads the device status block of the current device into words[0..3]
+ * ([0] first error code, [1] site, [2] block, [3] number of failures), after a
+ * synchronisation of the device, and clears it when `clear` is nonzero. */
+int kta_device_status(uint32_t* words, int clear);
+
+/* Number of SMs of the current device (the persistent grids' size). */
+int kta_sm_count(void);
+
+/* --- GEMM: C[M,N] = A[M,K] . B[N,K]^T, fp32 accumulate --------------------------------
+ * Replaces the TileLang `hgemm` case (perfmodel/testset/gen.py:255-303) and the seed GEMM
+ * family (knowledge/seed/families/gemm_fp16_tilelang/gen.py:32-112), launched like
+ * src/kta/measure/bench.py:94-98. Row-major A, B, C with leading dimensions lda, ldb, ldc
+ * in elements (each a multiple of 8, pointers 16-byte aligned). M = 16..64 runs the
+ * swap-AB split-K path (HBM-bound skinny shapes). */
+int kta_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                  int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+int kta_gemm_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                 int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+
+/* C[M,N] = A[M,K] . B[K,N] with B row-major K x N: the reference's own GEMM case statement
+ * `C = A @ B` (knowledge/seed/cases/gemm_fp16.yaml:8-13). Same rules as above. */
+int kta_gemm_nn_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                     int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+int kta_gemm_nn_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                    int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+
+/* --- FP8 block-scaled GEMM -------------------------------------------------------------
+ * C[M,N] (bf16) = sum_kb (A[:,kb] . B[:,kb]^T) * sa[m,kb] * sb[n/128,kb], with A [M,K] and
+ * B [N,K] e4m3 (row-major), sa [M, ceil(K/128)] fp32 (per 1x128 activation block) and
+ * sb [ceil(N/128), ceil(K/128)] fp32 (per 128x128 weight block). Replaces the TileLang
+ * `fp8gemm` (perfmodel/testset/gen.py:306-329), which has no scales. K % 16 == 0,
+ * N % 8 == 0. */
+int kta_gemm_fp8_blockscaled(const void* A, const void* sa, const void* B, const void* sb,
+                             void* C, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* --- Causal attention forward -----------------------------------------------------------
+ * O = softmax(Q K^T * scale + causal mask) V per (batch, head), LSE = logsumexp of the
+ * scaled, masked scores (natural log, fp32). Q, K, V, O bf16 in [B, S, H, D] layout (the
+ * layout of perfmodel/testset/gen.py:417-486); LSE fp32 [B, H, S]. D == 128. Replaces the
+ * TileLang `fa_forward` (non-causal there). */
+int kta_attn_fwd_causal_bf16(const void* Q, const void* K, const void* V, void* O, void* LSE,
+                             int64_t B, int64_t H, int64_t S, int64_t D, float scale,
+                             void* stream);
+
+/* --- GQA decode attention ---------------------------------------------------------------
+ * One query token per sequence: O[b,h,:] = softmax(Q[b,h,:] . K_b^T * scale) V_b with
+ * K_b = Kc[kv_offsets[b] : kv_offsets[b] + seqlens[b], h / (Hq/Hkv), :]. Q, O bf16
+ * [B, Hq, D]; Kc, Vc bf16 [total_tokens, Hkv, D] (each sequence contiguous); seqlens int32
+ * [B] and kv_offsets int64 [B] on the device. D == 128, Hq/Hkv == 4. The split-KV partials
+ * and their log-sum-exp combine (perfmodel/testset/gen.py:493-590) happen in one launch;
+ * `workspace` holds the partials and must be at least kta_decode_workspace_bytes(...)
+ * bytes, its counters zero before the first call (the kernel leaves them zero).
+ * max_seqlen bounds every seqlens[b]. */
+size_t kta_decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                                  int64_t max_seqlen);
+int kta_decode_gqa_bf16(const void* Q, const void* Kc, const void* Vc, const void* seqlens,
+                        const void* kv_offsets, void* O, int64_t B, int64_t Hq, int64_t Hkv,
+                        int64_t D, int64_t max_seqlen, float scale, void* workspace,
+                        size_t ws_bytes, void* stream);
+
+/* --- Reference-compatible `so` shims -----------------------------------------------------
+ * The exact signature src/kta/measure/bench.py:80-98 calls: pointers as uint64 device
+ * addresses, shape scalars as int32, restype None, default stream, the caller synchronises.
+ * Errors are recorded in the device status block's host mirror: read them with
+ * kta_last_error(). */
+void kta_so_gemm_bf16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K);
+void kta_so_gemm_f16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K);
+void kta_so_gemm_nn_f16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K);
+void kta_so_gemm_nn_bf16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K);
+
+/* Status of the last kta_so_* call on this host thread. */
+int kta_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KTA_B200_H */

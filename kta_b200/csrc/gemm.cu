@@ -1,0 +1,685 @@
+// 16-bit GEMM on the 5th-generation tensor cores (tcgen05), sm_100a.
+//
+//   C[M,N] = A[M,K] . op(B),  op(B) = B[N,K]^T ("tn", K-major B)  or  B[K,N] ("nn").
+//
+// It replaces KTA's TileLang hgemm (perfmodel/testset/gen.py:255-303) and the seed GEMM
+// family (knowledge/seed/families/gemm_fp16_tilelang/gen.py:32-112): same contraction,
+// fp32 accumulation, 16-bit output. The design is B200-first, not a translation:
+//
+//   * persistent grid of one CTA per SM walking a grouped raster of 128 x BN output tiles;
+//   * warp 0: TMA producer (128-byte swizzled K-major tiles into a STAGES-deep mbarrier
+//     ring); warp 1: TMEM allocator and the single-thread tcgen05.mma issuer;
+//     warps 2-5: epilogue (tcgen05.ld -> bf16/f16 -> swizzled smem -> TMA store);
+//   * the fp32 accumulator lives in TMEM, double buffered (2 x BN columns), so the
+//     epilogue of tile i overlaps the main loop of tile i+1;
+//   * every mbarrier wait is bounded (kta_common.cuh), no spin can hang the GPU.
+//
+// Skinny shapes (M <= 64, e.g. the decode-time M = 16) are HBM-bound on B: they run a
+// swap-AB kernel (D^T = B . A^T, UMMA M = 128 rows of B, N = M rounded up to 16) split
+// along K over a thread-block cluster whose partial sums are reduced through distributed
+// shared memory, so every SM streams B and no global workspace is needed.
+#include <algorithm>
+
+#include "kta_common.cuh"
+#include "kta_host.h"
+
+namespace kta {
+namespace gemm {
+
+constexpr int BM = 128;         // UMMA M (rows of A per tile)
+constexpr int BK = 64;          // 16-bit K elements per stage = one 128-byte swizzle row
+constexpr int UMMA_K = 16;      // K per tcgen05.mma of kind::f16
+constexpr int EPI_WARPS = 4;    // one per TMEM lane quarter
+constexpr int NUM_THREADS = 64 + EPI_WARPS * 32;
+constexpr int EPI_COLS = 64;    // output columns per staged chunk (128 B of 16-bit values)
+constexpr int GROUP_M = 16;     // raster group height (tiles) for L2 reuse
+
+// Watchdog sites (kta_device_status word 1).
+enum : unsigned int {
+  SITE_PRODUCER_EMPTY = 0x101,
+  SITE_MMA_FULL = 0x102,
+  SITE_MMA_TEMPTY = 0x103,
+  SITE_EPI_TFULL = 0x104,
+  SITE_SKINNY_FULL = 0x111,
+  SITE_SKINNY_EMPTY = 0x112,
+  SITE_SKINNY_TFULL = 0x113,
+};
+
+template <int BN, int STAGES>
+struct Layout {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int C_BYTES = 32 * EPI_COLS * 2;  // one warp's staged chunk
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_C = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_BAR = OFF_C + EPI_WARPS * 2 * C_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 4;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int TOTAL = OFF_MISC + 16;
+  static constexpr int ALLOC = TOTAL + 1024;  // slack to align the base to 1024 B
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static_assert(ALLOC <= 232448, "shared memory budget of one sm_100 CTA");
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb,
+                                            int& nb) {
+  const int per_group = GROUP_M * tiles_n;
+  const int group = tile / per_group;
+  const int first_m = group * GROUP_M;
+  const int gsz = min(tiles_m - first_m, GROUP_M);
+  const int r = tile - group * per_group;
+  mb = first_m + r % gsz;
+  nb = r / gsz;
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  const uint32_t a = smem_u32(p);
+  return p + ((1024u - (a & 1023u)) & 1023u);
+}
+
+// B_KMAJOR: B is [N,K] (tn); otherwise B is [K,N] (nn) and is fed as an MN-major operand.
+template <int BN, int STAGES, bool BF16, bool B_KMAJOR>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
+                unsigned int* status) {
+  using L = Layout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = warp_id();
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int tiles_m = (M + BM - 1) / BM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, tiles_m, tiles_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, SITE_PRODUCER_EMPTY)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + L::OFF_A + stage * L::A_BYTES;
+          uint8_t* sb = smem + L::OFF_B + stage * L::B_BYTES;
+          mbar_arrive_expect_tx(&full[stage], L::A_BYTES + L::B_BYTES);
+          tma_load_2d(&tmA, &full[stage], sa, kb * BK, mb * BM);
+          if constexpr (B_KMAJOR) {
+            tma_load_2d(&tmB, &full[stage], sb, kb * BK, nb * BN);
+          } else {
+            // [K,N] row-major: BN/64 boxes of 64 N x 64 K, each one MN-major swizzle block.
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              tma_load_2d(&tmB, &full[stage], sb + j * (64 * BK * 2), nb * BN + j * 64, kb * BK);
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t fmt = BF16 ? 1u : 0u;
+      constexpr uint32_t idesc = make_idesc(BM, BN, fmt, fmt, 0u, B_KMAJOR ? 0u : 1u);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, status, SITE_MMA_TEMPTY)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, status, SITE_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + L::OFF_A + stage * L::A_BYTES);
+          const uint32_t b0 = smem_u32(smem + L::OFF_B + stage * L::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            const uint64_t ad = sdesc_sw128(a0 + k * UMMA_K * 2, 16, 1024);
+            uint64_t bd;
+            if constexpr (B_KMAJOR) {
+              bd = sdesc_sw128(b0 + k * UMMA_K * 2, 16, 1024);
+            } else {
+              // K rows are 128 B apart: 16 K rows per MMA; 64-wide N blocks 8 KB apart.
+              bd = sdesc_sw128(b0 + k * UMMA_K * 128, 64 * BK * 2, 1024);
+            }
+            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);  // frees the smem stage once these MMAs completed
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);  // accumulator complete
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---------------- epilogue: TMEM -> registers -> smem -> TMA store ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    uint8_t* cbuf = smem + L::OFF_C + (warp - 2) * 2 * L::C_BYTES;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int buf = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, tiles_m, tiles_n, mb, nb);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, status, SITE_EPI_TFULL)) break;
+      tc_fence_after();
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / EPI_COLS; ++c) {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(t_row + c * EPI_COLS, r0);
+        tmem_ld_32x32b_x32(t_row + c * EPI_COLS + 32, r1);
+        tmem_ld_wait();
+        reg_fence(r0);
+        reg_fence(r1);
+        if (c == BN / EPI_COLS - 1) {
+          // Every column of this accumulator is in registers: hand TMEM back to the MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        uint32_t p[32];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          p[j] = pack2<BF16>(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1]));
+          p[16 + j] = pack2<BF16>(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1]));
+        }
+        // The store issued from this buffer two chunks ago must have finished reading it.
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        uint8_t* sbuf = cbuf + buf * L::C_BYTES;
+        const uint32_t row = smem_u32(sbuf) + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          st_shared_v4(row + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4), p[4 * j],
+                       p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, sbuf, nb * BN + c * EPI_COLS, mb * BM + q * 32);
+          bulk_commit_group();
+        }
+        buf ^= 1;
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Skinny M (<= 64): swap-AB, K split over a cluster, DSMEM reduction.
+// ---------------------------------------------------------------------------------------
+constexpr int SK_ROWS = 128;  // rows of B (columns of C) per CTA: UMMA M
+constexpr int SK_STAGES = 8;
+constexpr int SK_THREADS = NUM_THREADS;
+
+template <int MP>
+struct SkinnyLayout {
+  static constexpr int B_BYTES = SK_ROWS * BK * 2;  // "A operand": 128 rows of B
+  static constexpr int A_BYTES = MP * BK * 2;       // "B operand": MP rows of A
+  static constexpr int STAGE_BYTES = B_BYTES + ((A_BYTES + 1023) / 1024) * 1024;
+  static constexpr int OFF_STAGE = 0;
+  // [cluster-1][128][MP] fp32 partials; reuses the stage ring once every rank's main loop
+  // is over (the first cluster barrier of the epilogue).
+  static constexpr int OFF_RED = 0;
+  static constexpr int RED_SLOT_BYTES = SK_ROWS * MP * 4;
+  static constexpr int MAX_CLUSTER = (SK_STAGES * STAGE_BYTES) / RED_SLOT_BYTES + 1;
+  static constexpr int OFF_BAR = SK_STAGES * STAGE_BYTES;
+  static constexpr int OFF_MISC = OFF_BAR + (2 * SK_STAGES + 1) * 8;
+  static constexpr int TOTAL = OFF_MISC + 16;
+  static constexpr int ALLOC = TOTAL + 1024;
+  static constexpr uint32_t TMEM_COLS = MP <= 32 ? 32 : 64;
+  static_assert(ALLOC <= 232448, "shared memory budget of one sm_100 CTA");
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+template <int MP, bool BF16>
+__global__ void __launch_bounds__(SK_THREADS, 1)
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmA,
+                       const __grid_constant__ CUtensorMap tmB, void* __restrict__ Cv, int M,
+                       int N, int K, int64_t ldc, int csize, unsigned int* status) {
+  using L = SkinnyLayout<MP>;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = full + SK_STAGES;
+  uint64_t* tfull = empty + SK_STAGES;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
+
+  const int warp = warp_id();
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int tile = blockIdx.x / csize;
+  const int num_kb = (K + BK - 1) / BK;
+  const int kb_begin = static_cast<int>((static_cast<int64_t>(rank) * num_kb) / csize);
+  const int kb_end = static_cast<int>((static_cast<int64_t>(rank + 1) * num_kb) / csize);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SK_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // every CTA of the cluster runs before any DSMEM access
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, SITE_SKINNY_EMPTY)) break;
+        uint8_t* st = smem + L::OFF_STAGE + stage * L::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[stage], L::B_BYTES + L::A_BYTES);
+        tma_load_2d(&tmB, &full[stage], st, kb * BK, tile * SK_ROWS);
+        tma_load_2d(&tmA, &full[stage], st + L::B_BYTES, kb * BK, 0);
+        if (++stage == SK_STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t fmt = BF16 ? 1u : 0u;
+      constexpr uint32_t idesc = make_idesc(SK_ROWS, MP, fmt, fmt, 0u, 0u);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, status, SITE_SKINNY_FULL)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t s0 = smem_u32(smem + L::OFF_STAGE + stage * L::STAGE_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / UMMA_K; ++k) {
+          const uint64_t ad = sdesc_sw128(s0 + k * UMMA_K * 2, 16, 1024);
+          const uint64_t bd = sdesc_sw128(s0 + L::B_BYTES + k * UMMA_K * 2, 16, 1024);
+          umma_f16(tmem_base, ad, bd, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[stage]);
+        if (++stage == SK_STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) umma_commit(tfull);
+    }
+  }
+
+  // Epilogue warps (2-5) read the partial D^T tile: lane = row of B (column of C).
+  float acc[MP];
+  const bool epi = warp >= 2;
+  const int q = warp & 3;
+  const int row = q * 32 + lane;  // 0..127 within the tile
+  bool have = false;
+  if (epi) {
+    if (kb_end > kb_begin) {
+      if (mbar_wait(tfull, 0, abort_flag, status, SITE_SKINNY_TFULL)) {
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll
+        for (int c = 0; c < MP; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(taddr + c, r);
+          tmem_ld_wait();
+          reg_fence(r);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[c + j] = __uint_as_float(r[j]);
+        }
+        have = true;
+      }
+    }
+    if (!have) {
+#pragma unroll
+      for (int j = 0; j < MP; ++j) acc[j] = 0.f;
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // every rank's main loop is over: the stage rings are free
+  if (epi && rank != 0) {
+    // Send the partial to rank 0's reduction slot [rank-1][row][MP].
+    const uint32_t local = smem_u32(red + ((rank - 1) * SK_ROWS + row) * MP);
+    const uint32_t remote = map_to_rank(local, 0);
+#pragma unroll
+    for (int j = 0; j < MP; ++j) st_cluster_f32(remote + j * 4, acc[j]);
+  }
+  __syncwarp();
+  cluster_sync_all();  // partials of every rank are in rank 0's shared memory
+  if (epi && rank == 0) {
+    for (int r = 1; r < csize; ++r) {
+      const float* src = red + ((r - 1) * SK_ROWS + row) * MP;
+#pragma unroll
+      for (int j = 0; j < MP; ++j) acc[j] += src[j];
+    }
+    const int n = tile * SK_ROWS + row;
+    if (n < N) {
+      T* C = reinterpret_cast<T*>(Cv);
+#pragma unroll
+      for (int j = 0; j < MP; ++j) {
+        if (j < M) {
+          if constexpr (BF16) {
+            C[static_cast<int64_t>(j) * ldc + n] = __float2bfloat16_rn(acc[j]);
+          } else {
+            C[static_cast<int64_t>(j) * ldc + n] = __float2half_rn(acc[j]);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------
+template <typename Kern>
+int set_smem(Kern kernel, int bytes) {
+  return set_kernel_smem(reinterpret_cast<const void*>(kernel), bytes);
+}
+
+template <int BN, int STAGES, bool BF16, bool B_KMAJOR>
+int launch_main(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda,
+                int64_t ldb, int64_t ldc, cudaStream_t stream) {
+  using L = Layout<BN, STAGES>;
+  const CUtensorMapDataType dt =
+      BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb, tc;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+    const uint32_t box[2] = {BK, BM};
+    int s = encode_tmap(&ta, dt, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  }
+  if (B_KMAJOR) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t box[2] = {BK, BN};
+    int s = encode_tmap(&tb, dt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  } else {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t box[2] = {64, BK};
+    int s = encode_tmap(&tb, dt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldc) * 2};
+    const uint32_t box[2] = {EPI_COLS, 32};
+    int s = encode_tmap(&tc, dt, 2, C, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  }
+  auto kernel = gemm_kernel<BN, STAGES, BF16, B_KMAJOR>;
+  int s = set_smem(kernel, L::ALLOC);
+  if (s != KTA_OK) return s;
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int sms = current_sm_count();
+  const int grid = std::max(1, std::min(tiles, sms));
+  kernel<<<grid, NUM_THREADS, L::ALLOC, stream>>>(ta, tb, tc, M, N, K, device_status_ptr());
+  return launch_status();
+}
+
+template <int MP, bool BF16>
+int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda,
+                  int64_t ldb, int64_t ldc, cudaStream_t stream) {
+  using L = SkinnyLayout<MP>;
+  const CUtensorMapDataType dt =
+      BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+    const uint32_t box[2] = {BK, static_cast<uint32_t>(MP)};
+    int s = encode_tmap(&ta, dt, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t box[2] = {BK, SK_ROWS};
+    int s = encode_tmap(&tb, dt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  }
+  auto kernel = gemm_skinny_kernel<MP, BF16>;
+  int s = set_smem(kernel, L::ALLOC);
+  if (s != KTA_OK) return s;
+  const int tiles = (N + SK_ROWS - 1) / SK_ROWS;
+  const int num_kb = (K + BK - 1) / BK;
+  const int sms = current_sm_count();
+  // Cluster size: the largest power of two (<= 8) that keeps tiles x size within one wave
+  // and leaves every rank at least two k-blocks.
+  int cs = 1;
+  while (cs < 8 && cs * 2 <= L::MAX_CLUSTER && tiles * cs * 2 <= sms && num_kb >= cs * 4) {
+    cs *= 2;
+  }
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * cs), 1, 1);
+  cfg.blockDim = dim3(SK_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = L::ALLOC;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cs);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* Cp = C;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, Cp, M, N, K, ldc, cs,
+                                     device_status_ptr());
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return KTA_ERR_LAUNCH;
+  }
+  return launch_status();
+}
+
+// Estimated relative time of a tile width: waves x columns, discounted by how close the
+// tile runs to the shared-memory bandwidth limit (128x64 tiles feed the tensor core at
+// 192 B/clk against 128 B/clk available; 128x128 at 128; 128x256 at 96).
+inline double tile_cost(int M, int N, int BN, int sms) {
+  const double eff = BN == 256 ? 1.0 : (BN == 128 ? 0.9 : 0.6);
+  const long tiles = static_cast<long>((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const long waves = (tiles + sms - 1) / sms;
+  return static_cast<double>(waves) * BN / eff;
+}
+
+template <bool BF16, bool B_KMAJOR>
+int dispatch(const void* A, const void* B, void* C, int64_t M64, int64_t N64, int64_t K64,
+             int64_t lda, int64_t ldb, int64_t ldc, void* stream_v) {
+  if (A == nullptr || B == nullptr || C == nullptr) return KTA_ERR_INVALID_ARG;
+  if (M64 <= 0 || N64 <= 0 || K64 <= 0) return KTA_ERR_INVALID_ARG;
+  if (M64 > (1 << 30) || N64 > (1 << 30) || K64 > (1 << 30)) return KTA_ERR_UNSUPPORTED;
+  if (lda < K64 || ldc < N64 || (B_KMAJOR ? ldb < K64 : ldb < N64)) return KTA_ERR_INVALID_ARG;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C)) return KTA_ERR_ALIGN;
+  if (lda % 8 || ldb % 8 || ldc % 8) return KTA_ERR_ALIGN;
+  int s = require_sm100();
+  if (s != KTA_OK) return s;
+  const int M = static_cast<int>(M64), N = static_cast<int>(N64), K = static_cast<int>(K64);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (B_KMAJOR && M <= 64) {
+    if (M <= 16) return launch_skinny<16, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+    if (M <= 32) return launch_skinny<32, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+    if (M <= 48) return launch_skinny<48, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+    return launch_skinny<64, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+  }
+  const int sms = std::max(1, current_sm_count());
+  const double c256 = tile_cost(M, N, 256, sms);
+  const double c128 = tile_cost(M, N, 128, sms);
+  const double c64 = tile_cost(M, N, 64, sms);
+  if (c256 <= c128 && c256 <= c64) {
+    return launch_main<256, 4, BF16, B_KMAJOR>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+  }
+  if (c128 <= c64) {
+    return launch_main<128, 6, BF16, B_KMAJOR>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+  }
+  return launch_main<64, 8, BF16, B_KMAJOR>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+}
+
+}  // namespace gemm
+}  // namespace kta
+
+extern "C" {
+
+int kta_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                  int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  return kta::gemm::dispatch<true, true>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+}
+
+int kta_gemm_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                 int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  return kta::gemm::dispatch<false, true>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+}
+
+int kta_gemm_nn_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                     int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  return kta::gemm::dispatch<true, false>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+}
+
+int kta_gemm_nn_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                    int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  return kta::gemm::dispatch<false, false>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+}
+
+// Reference `so` module entries (src/kta/measure/bench.py:94-98): device addresses and
+// int32 shape scalars, dense row-major operands, default stream, no return value.
+void kta_so_gemm_bf16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K) {
+  kta::set_last_error(kta_gemm_bf16(reinterpret_cast<const void*>(A),
+                                    reinterpret_cast<const void*>(B),
+                                    reinterpret_cast<void*>(C), M, N, K, K, K, N, nullptr));
+}
+
+void kta_so_gemm_f16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K) {
+  kta::set_last_error(kta_gemm_f16(reinterpret_cast<const void*>(A),
+                                   reinterpret_cast<const void*>(B), reinterpret_cast<void*>(C),
+                                   M, N, K, K, K, N, nullptr));
+}
+
+void kta_so_gemm_nn_f16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K) {
+  kta::set_last_error(kta_gemm_nn_f16(reinterpret_cast<const void*>(A),
+                                      reinterpret_cast<const void*>(B),
+                                      reinterpret_cast<void*>(C), M, N, K, K, N, N, nullptr));
+}
+
+void kta_so_gemm_nn_bf16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K) {
+  kta::set_last_error(kta_gemm_nn_bf16(reinterpret_cast<const void*>(A),
+                                       reinterpret_cast<const void*>(B),
+                                       reinterpret_cast<void*>(C), M, N, K, K, N, N, nullptr));
+}
+
+}  // extern "C"

@@ -1,0 +1,45 @@
+// Host-side helpers shared by the entry points of libkta_b200 (runtime.cu implements them).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "kta_b200.h"
+
+namespace kta {
+
+// Device status block of the current device (4 words, see kta_device_status), or nullptr
+// when it cannot be resolved. Resolved once per device with that device current.
+unsigned int* device_status_ptr();
+
+// SM count of the current device (cached per device); 0 on error.
+int current_sm_count();
+
+// Compute capability major of the current device; -1 on error.
+int current_cc_major();
+
+// Encodes a tiled tensor map (rank 2 or 3) through the driver's cuTensorMapEncodeTiled,
+// resolved with cudaGetDriverEntryPoint (the library does not link libcuda).
+// dims/strides are innermost-first; strides_bytes holds rank-1 entries (dims 1..rank-1).
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                CUtensorMapSwizzle swizzle);
+
+// Maps the pending CUDA error of the last launch to a status code.
+int launch_status();
+
+// True if `p` is 16-byte aligned.
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Common device precondition of every entry: a device of compute capability 10.x.
+int require_sm100();
+
+// Raises the dynamic shared-memory limit of `kernel` to `bytes` on the current device
+// (once per kernel and device).
+int set_kernel_smem(const void* kernel, int bytes);
+
+// Status of the last kta_so_* call on this host thread (kta_last_error).
+void set_last_error(int s);
+
+}  // namespace kta

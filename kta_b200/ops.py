@@ -1,0 +1,158 @@
+"""Tensor-level wrappers over the C ABI (include/kta_b200.h) for torch CUDA tensors.
+
+Each function validates dtypes, shapes and devices, allocates the output with torch when
+none is given (torch is the caller's allocator here, the library allocates nothing), and
+launches on the current torch stream. Every call goes to libkta_b200; there is no other
+implementation behind these functions.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from kta_b200 import lib
+
+
+def _stream() -> int:
+    return int(torch.cuda.current_stream().cuda_stream)
+
+
+def _need_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("libkta_b200 operates on CUDA tensors only")
+
+
+def _rows_contig(t: torch.Tensor, name: str) -> None:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D tensor with unit column stride")
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, *,
+         b_layout: str = "nk") -> torch.Tensor:
+    """C = A @ B.T (``b_layout="nk"``, B is [N, K]) or C = A @ B (``"kn"``, B is [K, N]).
+
+    A, B, C are bf16 or f16 (all the same), row-major with unit column stride."""
+    _need_cuda(a, b)
+    _rows_contig(a, "A")
+    _rows_contig(b, "B")
+    if a.dtype != b.dtype or a.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("A and B must both be bf16 or both f16")
+    m, k = a.shape
+    if b_layout == "nk":
+        n, kb = b.shape
+    elif b_layout == "kn":
+        kb, n = b.shape
+    else:
+        raise ValueError("b_layout must be 'nk' or 'kn'")
+    if kb != k:
+        raise ValueError(f"K mismatch: A has {k}, B has {kb}")
+    if out is None:
+        out = torch.empty((m, n), dtype=a.dtype, device=a.device)
+    _rows_contig(out, "C")
+    if out.dtype != a.dtype or tuple(out.shape) != (m, n):
+        raise ValueError("C must match A's dtype and be [M, N]")
+    bf16 = a.dtype == torch.bfloat16
+    entry = {
+        ("nk", True): "kta_gemm_bf16",
+        ("nk", False): "kta_gemm_f16",
+        ("kn", True): "kta_gemm_nn_bf16",
+        ("kn", False): "kta_gemm_nn_f16",
+    }[(b_layout, bf16)]
+    lib.call(entry, a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k,
+             a.stride(0), b.stride(0), out.stride(0), _stream())
+    return out
+
+
+def gemm_fp8_blockscaled(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor,
+                         out: torch.Tensor | None = None) -> torch.Tensor:
+    """C (bf16) = dequant(A, sa) @ dequant(B, sb).T with per-1x128 activation scales sa
+    [M, ceil(K/128)] and per-128x128 weight scales sb [ceil(N/128), ceil(K/128)] (fp32)."""
+    _need_cuda(a, sa, b, sb)
+    if a.dtype != torch.float8_e4m3fn or b.dtype != torch.float8_e4m3fn:
+        raise ValueError("A and B must be float8_e4m3fn")
+    if sa.dtype != torch.float32 or sb.dtype != torch.float32:
+        raise ValueError("scales must be float32")
+    for t, name in ((a, "A"), (b, "B"), (sa, "sa"), (sb, "sb")):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    m, k = a.shape
+    n, kb = b.shape
+    if kb != k:
+        raise ValueError("K mismatch")
+    kblk, nblk = -(-k // 128), -(-n // 128)
+    if tuple(sa.shape) != (m, kblk) or tuple(sb.shape) != (nblk, kblk):
+        raise ValueError(f"scales must be sa [{m}, {kblk}] and sb [{nblk}, {kblk}]")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    if out.dtype != torch.bfloat16 or tuple(out.shape) != (m, n) or not out.is_contiguous():
+        raise ValueError("C must be a contiguous bf16 [M, N] tensor")
+    lib.call("kta_gemm_fp8_blockscaled", a.data_ptr(), sa.data_ptr(), b.data_ptr(),
+             sb.data_ptr(), out.data_ptr(), m, n, k, _stream())
+    return out
+
+
+def attn_fwd_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None,
+                    out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
+                    ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Causal attention forward. Q, K, V bf16 [B, S, H, D] contiguous; returns O bf16
+    [B, S, H, D] and LSE fp32 [B, H, S] (natural log)."""
+    _need_cuda(q, k, v)
+    for t, name in ((q, "Q"), (k, "K"), (v, "V")):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.dim() != 4:
+            raise ValueError(f"{name} must be a contiguous bf16 [B, S, H, D] tensor")
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("Q, K, V must have the same shape")
+    bsz, s, h, d = q.shape
+    if scale is None:
+        scale = d ** -0.5
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((bsz, h, s), dtype=torch.float32, device=q.device)
+    if out.shape != q.shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("O must be a contiguous bf16 tensor shaped like Q")
+    if tuple(lse.shape) != (bsz, h, s) or lse.dtype != torch.float32 or not lse.is_contiguous():
+        raise ValueError("LSE must be a contiguous fp32 [B, H, S] tensor")
+    lib.call("kta_attn_fwd_causal_bf16", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+             out.data_ptr(), lse.data_ptr(), bsz, h, s, d, float(scale), _stream())
+    return out, lse
+
+
+def decode_workspace_bytes(batch: int, hq: int, hkv: int, d: int, max_seqlen: int) -> int:
+    return int(lib.load().kta_decode_workspace_bytes(batch, hq, hkv, d, max_seqlen))
+
+
+def decode_gqa(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+               seqlens: torch.Tensor, kv_offsets: torch.Tensor, max_seqlen: int,
+               scale: float | None = None, out: torch.Tensor | None = None,
+               workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """GQA decode: Q bf16 [B, Hq, D]; caches bf16 [T, Hkv, D] with sequence b at rows
+    kv_offsets[b] .. kv_offsets[b] + seqlens[b]; seqlens int32 [B], kv_offsets int64 [B].
+    ``workspace`` (uint8, zero-initialised once) may be reused across calls on one stream."""
+    _need_cuda(q, k_cache, v_cache, seqlens, kv_offsets)
+    if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or \
+            v_cache.dtype != torch.bfloat16:
+        raise ValueError("Q and the caches must be bf16")
+    for t, name in ((q, "Q"), (k_cache, "K cache"), (v_cache, "V cache")):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if seqlens.dtype != torch.int32 or kv_offsets.dtype != torch.int64:
+        raise ValueError("seqlens must be int32 and kv_offsets int64")
+    bsz, hq, d = q.shape
+    hkv = k_cache.shape[1]
+    if k_cache.shape != v_cache.shape or k_cache.shape[2] != d:
+        raise ValueError("K and V caches must be [T, Hkv, D] with Q's D")
+    if scale is None:
+        scale = d ** -0.5
+    if out is None:
+        out = torch.empty_like(q)
+    need = decode_workspace_bytes(bsz, hq, hkv, d, max_seqlen)
+    if workspace is None:
+        workspace = torch.zeros(max(need, 1), dtype=torch.uint8, device=q.device)
+    if workspace.numel() < need:
+        raise ValueError(f"workspace needs {need} bytes")
+    lib.call("kta_decode_gqa_bf16", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+             seqlens.data_ptr(), kv_offsets.data_ptr(), out.data_ptr(), bsz, hq, hkv, d,
+             int(max_seqlen), float(scale), workspace.data_ptr(), workspace.numel(), _stream())
+    return out

@@ -1,0 +1,25 @@
+"""The oracle: a CPU restatement of the reference's algorithms for this path.
+
+TEST INFRASTRUCTURE ONLY. Only tests/, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU
+baseline leg (``--impl reference`` and the ``cpu_baseline`` field) import this package, and
+only as the checker or as the timed CPU reference implementation; the product path
+(kta_b200) never imports, calls or links anything here.
+
+Contents, each citing the reference code it restates (paths within kernel-template-agent):
+
+- ``numerics``: exact widening of bf16 / f16 / e4m3 bit patterns to float64 (numpy).
+- ``gemm``: the GEMM case statements ``C = A @ B`` (knowledge/seed/cases/gemm_fp16.yaml:8)
+  and ``C = A @ B.T`` evaluated in FP64 as src/kta/checks/scripts/ref_torch.py:28-38 does.
+- ``fp8``: the block-scaled FP8 statement (dequantise, then FP64 product) and the e4m3
+  quantiser of the input generator.
+- ``attention``: causal attention forward with log-sum-exp, and GQA decode with the
+  split-KV partial / log-sum-exp combine of perfmodel/testset/gen.py:417-590.
+- ``statement``: the reference's statement runner (ref_torch.py:17-45) on the CPU.
+
+Pinning: tests/golden holds fixtures generated in a container where the reference's Python
+is importable (tests/golden/make_golden.py): the reference's own input generators, its own
+ref_torch.py run on the CPU, and its compare_output / library_verdict / bound. The oracle is
+checked against them in tests/test_oracle_golden.py. Attention and block-scaled FP8 have no
+reference implementation or fixture: their parity is unpinned beyond the shared statement
+runner.
+"""
