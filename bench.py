@@ -1,0 +1,636 @@
+"""Throughput of the libkta_b200 hot path on 1..8 B200 GPUs (one process per GPU).
+
+Default workload: the bf16 GEMM case C = A . B^T at M = N = K = 8192 (kta_b200/cases/
+gemm_bf16_8192.yaml), sharded across ranks by N-column blocks of B (rank r owns rows
+[r N/n, (r+1) N/n) of B and the matching columns of C; A is replicated). No collective runs
+on the data path; the total work is fixed as N grows ("scaling": "strong").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kta|reference]
+                    [--workload gemm_bf16_8192|gemm_bf16_skinny|gemm_f16_1024|attn_causal|
+                                decode_gqa|gemm_fp8]
+
+A step is one launch of the hot-path kernel over one rotating input set already resident in
+HBM (4 sets; every workload's inputs exceed the 126 MB L2, so no flush is needed between
+steps). Rank 0 prints one JSON line: the driver's keys plus `roofline` (the dominant kernel's
+achieved rate from CUDA events against MEASURED_PEAKS.json), `sol` (the case's L1
+speed-of-light bound, as KTA reports pct_of_bound), `e2e` (the same metric through the
+public API with pinned host inputs copied in and the result copied out every step),
+`cpu_baseline` (the reference's CPU torch path timed on a bounded sample) and `clocks`.
+
+`--impl reference` times the reference's own CPU implementation of the path instead: the
+case statement run by torch on the host cores in the inputs' dtype, i.e. the "library"
+statement of src/kta/checks/scripts/ref_torch.py:39-43 with the device set to cpu, each
+step a bounded sample of the workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GEMM/attention TFLOP/s (decode: HBM GB/s) & % of SOL at 1/2/4/8 B200"
+NSETS = 4
+CPU_BUDGET_S = 12.0  # CPU baseline sample: about this much host compute
+
+
+# ---------------------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------------------
+class Dist:
+    def __init__(self, want: int) -> None:
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if want > 1 and self.world != want:
+            raise SystemExit(f"--gpus {want} needs torchrun with {want} ranks (WORLD_SIZE="
+                             f"{self.world})")
+        self.pg = None
+
+    def init(self) -> None:
+        if self.world > 1:
+            import datetime
+
+            torch.distributed.init_process_group(
+                "nccl", timeout=datetime.timedelta(seconds=120),
+                device_id=torch.device("cuda", self.local))
+            self.pg = True
+
+    def barrier(self) -> None:
+        if self.pg:
+            torch.distributed.barrier(device_ids=[self.local])
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x: float) -> float:
+        if not self.pg:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.pg:
+            torch.distributed.destroy_process_group()
+
+
+def shard(n: int, parts: int, i: int, align: int = 1) -> tuple[int, int]:
+    """[lo, hi) of part i when n is split into `parts` blocks aligned to `align`."""
+    units = -(-n // align)
+    lo = (units * i) // parts * align
+    hi = min(n, (units * (i + 1)) // parts * align)
+    return lo, hi
+
+
+# ---------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self) -> None:
+        self.samples: list[tuple[float, dict[str, str]]] = []
+        self.proc: subprocess.Popen | None = None
+        self.thread: threading.Thread | None = None
+        self.bus: tuple[int, int, int] | None = None
+        try:
+            p = torch.cuda.get_device_properties(torch.cuda.current_device())
+            self.bus = (int(p.pci_domain_id), int(p.pci_bus_id), int(p.pci_device_id))
+        except Exception:
+            self.bus = None
+
+    def _mine(self, s: dict[str, str]) -> bool:
+        if self.bus is None:
+            return True
+        try:  # nvidia-smi prints domain:bus:device.function in hex
+            dom, bus, devfn = s["pci.bus_id"].split(":")
+            return (int(dom, 16), int(bus, 16), int(devfn.split(".")[0], 16)) == self.bus
+        except (KeyError, ValueError):
+            return False
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        keys = self.FIELDS.split(",")
+
+        def reader() -> None:
+            assert self.proc is not None and self.proc.stdout is not None
+            for line in self.proc.stdout:
+                vals = [v.strip() for v in line.split(",")]
+                if len(vals) == len(keys):
+                    self.samples.append((time.time(), dict(zip(keys, vals))))
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+
+    def stop(self) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        mine = [s for t, s in self.samples if self._mine(s)]
+        inside = [s for t, s in self.samples if t0 - 0.15 <= t <= t1 + 0.15 and self._mine(s)]
+        use = inside or mine[-3:]
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+        def num(s: dict, k: str) -> float | None:
+            try:
+                return float(s[k])
+            except (ValueError, KeyError):
+                return None
+
+        sm = [v for v in (num(s, "clocks.sm") for s in use) if v is not None]
+        reasons = set()
+        for s in use:
+            for k in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                      "sw_power_cap"):
+                if s.get(f"clocks_event_reasons.{k}", "").strip().lower() == "active":
+                    reasons.add(k)
+        power = [v for v in (num(s, "power.draw") for s in use) if v is not None]
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": num(use[0], "clocks.max.sm"),
+            "reasons": sorted(reasons),
+            "power_w_max": max(power) if power else None,
+            "samples": len(use),
+            "samples_in_timed_region": len(inside),
+        }
+
+
+# ---------------------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------------------
+def _randn(shape, dtype, gen, scale=1.0, device="cuda"):
+    x = torch.randn(*shape, generator=gen, device=device, dtype=torch.float32)
+    if scale != 1.0:
+        x.mul_(scale)
+    return x.to(dtype)
+
+
+class GemmWorkload:
+    """C = A . B^T (bf16/f16), this rank's N-column shard of B."""
+
+    kernel_regex = "gemm"
+
+    def __init__(self, name: str, m: int, n: int, k: int, dtype: torch.dtype, dist: Dist,
+                 case: str) -> None:
+        self.name, self.m, self.n_total, self.k, self.dtype = name, m, n, k, dtype
+        self.case = case
+        lo, hi = shard(n, dist.world, dist.rank, align=128)
+        self.n0, self.n = lo, hi - lo
+        self.esize = 2
+        self.hbm_bound = m <= 64
+        self.unit = "GB/s" if self.hbm_bound else "TFLOP/s"
+        self.dtype_name = "bf16" if dtype == torch.bfloat16 else "f16"
+        # a 1024^3 GEMM runs for a few microseconds: shorter than the host's launch path
+        self.graph_default = 2.0 * m * n * k < 2e10
+
+    @property
+    def flops(self) -> float:
+        return 2.0 * self.m * self.n * self.k
+
+    @property
+    def bytes(self) -> float:
+        return float((self.m * self.k + self.n * self.k + self.m * self.n) * self.esize)
+
+    def work(self) -> float:  # this rank's units of the metric per step
+        return self.bytes if self.hbm_bound else self.flops
+
+    def sol_shape(self) -> dict:
+        return {"M": self.m, "N": self.n, "K": self.k}
+
+    def config(self, world: int) -> dict:
+        return {
+            "workload": f"{self.name}: C = A . B^T, {self.dtype_name}, M={self.m} N={self.n_total} "
+                        f"K={self.k}, fp32 accumulate",
+            "case": self.case,
+            "M": self.m, "N": self.n_total, "K": self.k,
+            "global_batch": self.m, "seq_len": None,
+            "parallelism": f"N-column shards x{world} (no collective)",
+            "l2": "inputs larger than L2 (126 MB): 4 rotating input sets, no flush",
+            "inputs": "N(0,1)/sqrt(K) from a seeded torch generator",
+        }
+
+    def setup(self, device: torch.device) -> None:
+        g = torch.Generator(device=device).manual_seed(1234)
+        s = 1.0 / math.sqrt(self.k)
+        self.a = [_randn((self.m, self.k), self.dtype, g, s) for _ in range(NSETS)]
+        self.b = [_randn((self.n, self.k), self.dtype, g, s) for _ in range(NSETS)]
+        self.c = [torch.empty((self.m, self.n), dtype=self.dtype, device=device)
+                  for _ in range(NSETS)]
+
+    def launch(self, i: int) -> None:
+        from kta_b200 import ops
+
+        j = i % NSETS
+        ops.gemm(self.a[j], self.b[j], out=self.c[j])
+
+    # ---- end to end: pinned host inputs in, result out, every step ----
+    def setup_e2e(self, device: torch.device) -> None:
+        g = torch.Generator().manual_seed(99)
+        s = 1.0 / math.sqrt(self.k)
+        self.ha = _randn((self.m, self.k), self.dtype, g, s, device="cpu").pin_memory()
+        self.hb = _randn((self.n, self.k), self.dtype, g, s, device="cpu").pin_memory()
+        self.hc = torch.empty((self.m, self.n), dtype=self.dtype).pin_memory()
+        self.da = torch.empty_like(self.ha, device=device)
+        self.db = torch.empty_like(self.hb, device=device)
+        self.dc = torch.empty_like(self.hc, device=device)
+        self.h2d_bytes = self.ha.numel() * self.esize + self.hb.numel() * self.esize
+        self.d2h_bytes = self.hc.numel() * self.esize
+
+    def e2e_step(self) -> None:
+        from kta_b200 import ops
+
+        self.da.copy_(self.ha, non_blocking=True)
+        self.db.copy_(self.hb, non_blocking=True)
+        ops.gemm(self.da, self.db, out=self.dc)
+        self.hc.copy_(self.dc, non_blocking=True)
+
+    # ---- the reference's CPU torch path on a bounded sample ----
+    def cpu_sample(self, rows: int):
+        g = torch.Generator().manual_seed(7)
+        s = 1.0 / math.sqrt(self.k)
+        a = _randn((rows, self.k), self.dtype, g, s, device="cpu")
+        b = _randn((self.n_total, self.k), self.dtype, g, s, device="cpu")
+
+        def run():
+            from oracle import statement
+
+            statement.run_library("C = A @ B.T", {"A": a, "B": b}, {})
+
+        units = (2.0 * rows * self.n_total * self.k if not self.hbm_bound
+                 else float((rows * self.k + self.n_total * self.k + rows * self.n_total) * 2))
+        return run, units, f"C = A @ B.T in {self.dtype_name} on the host, M={rows} rows of " \
+                           f"A (of {self.m}), N={self.n_total}, K={self.k}"
+
+
+WORKLOADS = {
+    "gemm_bf16_8192": lambda d: GemmWorkload("gemm_bf16_8192", 8192, 8192, 8192,
+                                             torch.bfloat16, d, "gemm_bf16_8192"),
+    "gemm_bf16_skinny": lambda d: GemmWorkload("gemm_bf16_skinny", 16, 8192, 8192,
+                                               torch.bfloat16, d, "gemm_bf16_8192"),
+    "gemm_f16_1024": lambda d: GemmWorkload("gemm_f16_1024", 1024, 1024, 1024,
+                                            torch.float16, d, "gemm_f16_1024"),
+}
+
+
+def _extra_workloads() -> None:
+    try:
+        from kta_b200 import bench_workloads  # attention, decode, fp8 (when built)
+    except ImportError:
+        return
+    WORKLOADS.update(bench_workloads.WORKLOADS)
+
+
+# ---------------------------------------------------------------------------------------
+# measurement
+# ---------------------------------------------------------------------------------------
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", 0) or 0),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback (profiling recipe: 6.65 TB/s, 1.59 PFLOP/s)"}
+
+
+def traffic_for(workload: str) -> float | None:
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    e = d.get(workload)
+    return float(e["dram_bytes_per_launch"]) if e else None
+
+
+def time_device(wl, steps: int, warmup: int, dist: Dist) -> dict:
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        wl.launch(i)
+    # keep the GPU busy for ~0.5 s more so clocks settle and the sampler is running
+    torch.cuda.synchronize()
+    t_w = time.perf_counter()
+    i = 0
+    while time.perf_counter() - t_w < 0.5:
+        wl.launch(i)
+        i += 1
+        if i % 8 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    wall0 = time.time()
+    evs[0].record(stream)
+    for s in range(steps):
+        wl.launch(s)
+        evs[s + 1].record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    dist.barrier()
+    torch.cuda.synchronize()
+    per = [evs[s].elapsed_time(evs[s + 1]) for s in range(steps)]
+    total_ms = evs[0].elapsed_time(evs[steps])
+    return {"total_ms": total_ms, "per_launch_ms": per, "wall": (wall0, wall1)}
+
+
+def time_device_graph(wl, steps: int, warmup: int, dist: Dist) -> dict:
+    """The K steps captured once into a CUDA graph and replayed: for launch-bound workloads
+    whose kernels are shorter than the host's launch path."""
+    for i in range(warmup):
+        wl.launch(i)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for s in range(steps):
+                wl.launch(s)
+    torch.cuda.synchronize()
+    graph.replay()  # warm replay
+    t_w = time.perf_counter()
+    while time.perf_counter() - t_w < 0.5:
+        graph.replay()
+        torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    dist.barrier()
+    total = e0.elapsed_time(e1)
+    del graph
+    return {"total_ms": total, "per_launch_ms": [total / steps] * steps, "wall": (wall0, wall1),
+            "graph": True}
+
+
+def time_e2e(wl, steps: int, dist: Dist) -> dict:
+    stream = torch.cuda.current_stream()
+    for _ in range(2):
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        wl.e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return {"total_ms": e0.elapsed_time(e1)}
+
+
+def calibrate_cpu(wl, budget_s: float):
+    """A sample of the workload (rows of the first operand, then repeats of the whole
+    workload) sized to about ``budget_s`` seconds of host compute."""
+    full = getattr(wl, "m", 8)
+    rows = min(8, full)
+    run, units, sample = wl.cpu_sample(rows)
+    run()  # first call pays library initialisation
+    while True:
+        t = time.perf_counter()
+        run()
+        dt = max(time.perf_counter() - t, 1e-6)
+        if dt >= 0.25 or rows >= full:
+            break
+        rows = min(full, rows * 4)
+        run, units, sample = wl.cpu_sample(rows)
+    if rows < full:
+        new_rows = min(full, max(8, int(rows * budget_s / dt) // 8 * 8))
+        dt = dt * new_rows / rows
+        rows = new_rows
+        run, units, sample = wl.cpu_sample(rows)
+    repeats = max(1, int(budget_s / dt)) if rows >= full else 1
+    return run, units, sample, repeats
+
+
+def cpu_baseline(wl, budget_s: float) -> dict:
+    """The reference's CPU torch path timed on a bounded sample of ~budget_s seconds."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    run, units, sample, repeats = calibrate_cpu(wl, budget_s)
+    t = time.perf_counter()
+    for _ in range(repeats):
+        run()
+    dt = time.perf_counter() - t
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    return {"value": units * repeats / dt / scale, "unit": wl.unit,
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{sample}; {repeats} repetition(s)", "seconds": round(dt, 3),
+            "host_cpus": os.cpu_count()}
+
+
+def run_kta(args, dist: Dist) -> dict | None:
+    from kta_b200 import bound as kbound, lib, schemas
+
+    device = torch.device("cuda", dist.local)
+    torch.cuda.set_device(device)
+    dist.init()
+    lib.load()
+    wl = WORKLOADS[args.workload](dist)
+    wl.setup(device)
+    if args.profile:
+        # exactly W + K launches of the hot-path kernel, nothing else (for ncu captures)
+        for i in range(args.warmup + args.steps):
+            wl.launch(i)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": args.workload, "launches": args.warmup + args.steps}))
+        return None
+    use_graph = args.graph or getattr(wl, "graph_default", False)
+    clocks = Clocks()
+    clocks.start()
+    if use_graph:
+        dev = time_device_graph(wl, args.steps, args.warmup, dist)
+    else:
+        dev = time_device(wl, args.steps, args.warmup, dist)
+    clocks.stop()
+    ms_total = dist.max(dev["total_ms"])
+    world_work = dist.sum(wl.work())
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    value = world_work * args.steps / (ms_total / 1e3) / scale
+    per = sorted(dev["per_launch_ms"])
+    mean_launch_ms = sum(per) / len(per)
+    pk = peaks()
+    peak = pk["bf16_tflops"] if wl.unit == "TFLOP/s" else pk["hbm_gbs"]
+    peak_note = "bf16_tflops (burst)" if wl.unit == "TFLOP/s" else "hbm_gbs"
+    if getattr(wl, "peak_key", None) == "fp8":
+        peak, peak_note = 2 * pk["bf16_tflops"], "2 x bf16_tflops (dense fp8 = 2x bf16 rate)"
+    achieved = wl.work() / (mean_launch_ms / 1e3) / scale
+    traffic = traffic_for(args.workload)
+    roofline = {
+        "kernel": wl.kernel_regex,
+        "bound": "tensor" if wl.unit == "TFLOP/s" else "hbm",
+        "achieved": round(achieved, 2),
+        "peak": peak,
+        "unit": wl.unit,
+        "frac": round(achieved / peak, 4),
+        "peak_source": f"{pk['source']}: {peak_note}",
+        "traffic": traffic,
+        "algorithmic_bytes_per_launch": wl.bytes,
+        "algorithmic_flops_per_launch": getattr(wl, "flops", None),
+        "mean_launch_ms": round(mean_launch_ms, 5),
+        "timing": "one CUDA graph of the K launches, total / K" if use_graph else
+                  "CUDA events between consecutive launches on the launching stream",
+        "median_launch_ms": round(statistics.median(per), 5),
+    }
+    # KTA's L1 speed-of-light bound of this rank's shard, as pct_of_bound
+    cf = schemas.load_case_file(wl.case)
+    hw = kbound.b200_model()
+    sol = kbound.sol_report(cf.problem, wl.sol_shape(), statistics.median(per) * 1e3, hw)
+    # end to end through the public API with host buffers
+    wl.setup_e2e(device)
+    e2e_steps = max(3, min(args.steps, 20))
+    e2e = time_e2e(wl, e2e_steps, dist)
+    e2e_ms = dist.max(e2e["total_ms"])
+    e2e_value = world_work * e2e_steps / (e2e_ms / 1e3) / scale
+    result = None
+    if dist.rank == 0:
+        cpu = cpu_baseline(wl, CPU_BUDGET_S) if dist.world == 1 else None
+        ck = clocks.summary(*dev["wall"])
+        result = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": wl.unit,
+            "n_gpus": dist.world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_total / args.steps, 5),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": wl.dtype_name,
+            "data": "synthetic (seeded N(0,1)/sqrt(K) per the case)",
+            "config": wl.config(dist.world),
+            "impl": "kta",
+            "roofline": roofline,
+            "sol": {"pct_of_bound": round(sol["pct_of_bound"], 2), "bound_us": sol["bound_us"],
+                    "bottleneck": sol["bottleneck"], "near_bound": sol["near_bound"],
+                    "per_rank_shape": wl.sol_shape(), "peak_sources": sol["peak_sources"]},
+            "e2e": {"value": round(e2e_value, 3), "unit": wl.unit,
+                    "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
+                    "steps": e2e_steps,
+                    "path": "pinned host -> device copies, libkta_b200 C-ABI launch, "
+                            "device -> pinned host copy, every step"},
+            "cpu_baseline": cpu,
+            "clocks": ck,
+            "gpu_launches": args.steps,
+        }
+    return result
+
+
+def run_reference(args, dist: Dist) -> dict | None:
+    """The reference's CPU implementation of the path (the case statement in the inputs'
+    dtype through torch on the host cores); rank 0 only."""
+    if dist.rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    wl = WORKLOADS[args.workload](Dist(1))
+    budget_per_step = max(0.05, 150.0 / max(1, args.steps + args.warmup))
+    run, units, sample, repeats = calibrate_cpu(wl, budget_per_step)
+    units *= repeats
+    sample = f"{sample}; {repeats} repetition(s)"
+
+    def step() -> None:
+        for _ in range(repeats):
+            run()
+
+    for _ in range(args.warmup):
+        step()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    value = units * args.steps / dt / scale
+    return {
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": wl.unit,
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": wl.dtype_name,
+        "data": "synthetic (seeded N(0,1)/sqrt(K) per the case)",
+        "config": wl.config(1),
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads,
+                         "kind": "port", "sample": f"per step: {sample}"},
+        "e2e": {"value": round(value, 4), "unit": wl.unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> int:
+    _extra_workloads()
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["kta", "reference"], default="kta")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm_bf16_8192")
+    ap.add_argument("--graph", action="store_true",
+                    help="time the K steps as one CUDA graph replay (launch-bound workloads)")
+    ap.add_argument("--profile", action="store_true",
+                    help="run W + K launches of the kernel only (the command for ncu captures)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    dist = Dist(args.gpus)
+    if args.impl == "reference":
+        out = run_reference(args, dist)
+    else:
+        out = run_kta(args, dist)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+    if args.impl == "kta":
+        dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
