@@ -42,7 +42,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "GEMM/attention TFLOP/s (decode: HBM GB/s) & % of SOL at 1/2/4/8 B200"
-NSETS = 4
+NSETS = int(os.environ.get("KTA_BENCH_SETS", "4"))  # rotating input sets (1 for ncu captures)
 CPU_BUDGET_S = 12.0  # CPU baseline sample: about this much host compute
 
 
@@ -293,6 +293,148 @@ class GemmWorkload:
                            f"A (of {self.m}), N={self.n_total}, K={self.k}"
 
 
+def lpt(weights: list[int], parts: int) -> list[list[int]]:
+    """Greedy longest-processing-time assignment of items to `parts` bins."""
+    bins: list[list[int]] = [[] for _ in range(parts)]
+    load = [0] * parts
+    for i in sorted(range(len(weights)), key=lambda j: -weights[j]):
+        t = min(range(parts), key=lambda r: load[r])
+        bins[t].append(i)
+        load[t] += weights[i]
+    return [sorted(b) for b in bins]
+
+
+class DecodeWorkload:
+    """GQA decode: B=64, Hq=32, Hkv=8, D=128, lengths uniform in [1024, 8192] (seed 0);
+    this rank's sequences by LPT on length."""
+
+    kernel_regex = "decode_kernel"
+    unit = "GB/s"
+    dtype_name = "bf16"
+    case = "decode_gqa"
+    graph_default = False
+
+    def __init__(self, dist: Dist, batch: int = 64, hq: int = 32, hkv: int = 8, d: int = 128,
+                 lo: int = 1024, hi: int = 8192) -> None:
+        import numpy as np
+
+        self.batch, self.hq, self.hkv, self.d, self.max_seqlen = batch, hq, hkv, d, hi
+        lengths = np.random.default_rng(0).integers(lo, hi + 1, size=batch)
+        self.all_lengths = [int(x) for x in lengths]
+        mine = lpt(self.all_lengths, dist.world)[dist.rank]
+        self.lengths = [self.all_lengths[i] for i in mine]
+        self.b = len(self.lengths)
+        self.tokens = sum(self.lengths)
+
+    @property
+    def bytes(self) -> float:
+        return float(2 * self.tokens * self.hkv * self.d * 2 + 2 * self.b * self.hq * self.d * 2
+                     + self.b * 12)
+
+    flops = None
+
+    def work(self) -> float:
+        return self.bytes
+
+    def sol_shape(self) -> dict:
+        return {"B": self.b, "Hq": self.hq, "Hkv": self.hkv, "D": self.d, "T": self.tokens,
+                "max_seqlen": self.max_seqlen}
+
+    def config(self, world: int) -> dict:
+        return {"workload": f"decode_gqa: B={self.batch} Hq={self.hq} Hkv={self.hkv} D={self.d}, "
+                            f"one query token, KV lengths U[1024, 8192] (seed 0), bf16 cache",
+                "case": self.case, "B": self.batch, "Hq": self.hq, "Hkv": self.hkv, "D": self.d,
+                "kv_tokens": sum(self.all_lengths), "global_batch": self.batch, "seq_len": None,
+                "parallelism": f"sequences by LPT on length x{world} (no collective)",
+                "l2": "inputs larger than L2: 4 rotating KV caches, no flush",
+                "inputs": "N(0,1) bf16 from a seeded torch generator"}
+
+    def _offsets(self):
+        import numpy as np
+
+        return np.concatenate([[0], np.cumsum(self.lengths)[:-1]]).astype(np.int64)
+
+    def setup(self, device: torch.device) -> None:
+        from kta_b200 import ops
+
+        g = torch.Generator(device=device).manual_seed(4321)
+        self.q = [_randn((self.b, self.hq, self.d), torch.bfloat16, g) for _ in range(NSETS)]
+        self.kc = [_randn((self.tokens, self.hkv, self.d), torch.bfloat16, g) for _ in range(NSETS)]
+        self.vc = [_randn((self.tokens, self.hkv, self.d), torch.bfloat16, g) for _ in range(NSETS)]
+        self.sl = torch.tensor(self.lengths, dtype=torch.int32, device=device)
+        self.off = torch.tensor(self._offsets(), dtype=torch.int64, device=device)
+        self.o = [torch.empty_like(self.q[0]) for _ in range(NSETS)]
+        nbytes = ops.decode_workspace_bytes(self.b, self.hq, self.hkv, self.d, self.max_seqlen)
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
+    def launch(self, i: int) -> None:
+        from kta_b200 import ops
+
+        j = i % NSETS
+        ops.decode_gqa(self.q[j], self.kc[j], self.vc[j], self.sl, self.off, self.max_seqlen,
+                       out=self.o[j], workspace=self.ws)
+
+    def setup_e2e(self, device: torch.device) -> None:
+        g = torch.Generator().manual_seed(99)
+        self.hq_ = _randn((self.b, self.hq, self.d), torch.bfloat16, g, device="cpu").pin_memory()
+        self.hk = _randn((self.tokens, self.hkv, self.d), torch.bfloat16, g,
+                         device="cpu").pin_memory()
+        self.hv = _randn((self.tokens, self.hkv, self.d), torch.bfloat16, g,
+                         device="cpu").pin_memory()
+        self.hsl = torch.tensor(self.lengths, dtype=torch.int32).pin_memory()
+        self.hoff = torch.tensor(self._offsets(), dtype=torch.int64).pin_memory()
+        self.ho = torch.empty((self.b, self.hq, self.d), dtype=torch.bfloat16).pin_memory()
+        self.dq, self.dk, self.dv = (torch.empty_like(t, device=device)
+                                     for t in (self.hq_, self.hk, self.hv))
+        self.dsl = torch.empty_like(self.hsl, device=device)
+        self.doff = torch.empty_like(self.hoff, device=device)
+        self.do = torch.empty_like(self.ho, device=device)
+        self.h2d_bytes = sum(t.numel() * t.element_size()
+                             for t in (self.hq_, self.hk, self.hv, self.hsl, self.hoff))
+        self.d2h_bytes = self.ho.numel() * 2
+
+    def e2e_step(self) -> None:
+        from kta_b200 import ops
+
+        for dst, src in ((self.dq, self.hq_), (self.dk, self.hk), (self.dv, self.hv),
+                         (self.dsl, self.hsl), (self.doff, self.hoff)):
+            dst.copy_(src, non_blocking=True)
+        ops.decode_gqa(self.dq, self.dk, self.dv, self.dsl, self.doff, self.max_seqlen,
+                       out=self.do, workspace=self.ws)
+        self.ho.copy_(self.do, non_blocking=True)
+
+    def cpu_sample(self, nseq: int):
+        """The decode case statement in bf16 on the host for the first `nseq` sequences."""
+        nseq = max(1, min(nseq, self.b))
+        lens = self.lengths[:nseq]
+        g = torch.Generator().manual_seed(7)
+        tot = sum(lens)
+        q = _randn((nseq, self.hq, self.d), torch.bfloat16, g, device="cpu")
+        kc = _randn((tot, self.hkv, self.d), torch.bfloat16, g, device="cpu")
+        vc = _randn((tot, self.hkv, self.d), torch.bfloat16, g, device="cpu")
+        import numpy as np
+
+        off = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+        inputs = {"Q": q, "Kc": kc, "Vc": vc, "seqlens": torch.tensor(lens, dtype=torch.int32),
+                  "kv_offsets": torch.tensor(off)}
+        shape = {"B": nseq, "Hq": self.hq, "Hkv": self.hkv, "D": self.d}
+
+        def run():
+            from kta_b200 import schemas
+            from oracle import statement
+
+            stmt = schemas.load_case_file("decode_gqa").problem.reference_impl
+            statement.run_library(stmt, inputs, shape, ["O"])
+
+        units = float(2 * tot * self.hkv * self.d * 2 + 2 * nseq * self.hq * self.d * 2)
+        return run, units, (f"decode statement in bf16 on the host for {nseq} of {self.b} "
+                            f"sequences ({tot} KV tokens)")
+
+    @property
+    def m(self) -> int:  # the CPU calibration grows the sample up to all sequences
+        return self.b
+
+
 WORKLOADS = {
     "gemm_bf16_8192": lambda d: GemmWorkload("gemm_bf16_8192", 8192, 8192, 8192,
                                              torch.bfloat16, d, "gemm_bf16_8192"),
@@ -300,6 +442,7 @@ WORKLOADS = {
                                                torch.bfloat16, d, "gemm_bf16_8192"),
     "gemm_f16_1024": lambda d: GemmWorkload("gemm_f16_1024", 1024, 1024, 1024,
                                             torch.float16, d, "gemm_f16_1024"),
+    "decode_gqa": lambda d: DecodeWorkload(d),
 }
 
 

@@ -98,7 +98,10 @@ int kta_attn_fwd_causal_bf16(const void* Q, const void* K, const void* V, void* 
  * One query token per sequence: O[b,h,:] = softmax(Q[b,h,:] . K_b^T * scale) V_b with
  * K_b = Kc[kv_offsets[b] : kv_offsets[b] + seqlens[b], h / (Hq/Hkv), :]. Q, O bf16
  * [B, Hq, D]; Kc, Vc bf16 [total_tokens, Hkv, D] (each sequence contiguous); seqlens int32
- * [B] and kv_offsets int64 [B] on the device. D == 128, Hq/Hkv == 4. The split-KV partials
+ * [B] and kv_offsets int64 [B] on the device; cache_tokens = T bounds every
+ * kv_offsets[b] + seqlens[b] and max_seqlen every seqlens[b] (checked on the device: a
+ * sequence outside them gets a zero output and status KTA_ERR_DEVICE_BOUNDS in the device
+ * status block). D == 128, Hq/Hkv <= 16, B <= 2048. The split-KV partials
  * and their log-sum-exp combine (perfmodel/testset/gen.py:493-590) happen in one launch;
  * `workspace` holds the partials and must be at least kta_decode_workspace_bytes(...)
  * bytes, its counters zero before the first call (the kernel leaves them zero).
@@ -107,8 +110,8 @@ size_t kta_decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
                                   int64_t max_seqlen);
 int kta_decode_gqa_bf16(const void* Q, const void* Kc, const void* Vc, const void* seqlens,
                         const void* kv_offsets, void* O, int64_t B, int64_t Hq, int64_t Hkv,
-                        int64_t D, int64_t max_seqlen, float scale, void* workspace,
-                        size_t ws_bytes, void* stream);
+                        int64_t D, int64_t cache_tokens, int64_t max_seqlen, float scale,
+                        void* workspace, size_t ws_bytes, void* stream);
 
 /* --- Reference-compatible `so` shims -----------------------------------------------------
  * The exact signature src/kta/measure/bench.py:80-98 calls: pointers as uint64 device

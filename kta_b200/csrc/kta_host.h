@@ -36,7 +36,7 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 int require_sm100();
 
 // Raises the dynamic shared-memory limit of `kernel` to `bytes` on the current device
-// (once per kernel and device).
+// (once per kernel and device: pass the largest size any launch of `kernel` will use).
 int set_kernel_smem(const void* kernel, int bytes);
 
 // Status of the last kta_so_* call on this host thread (kta_last_error).

@@ -14,12 +14,4 @@ int kta_attn_fwd_causal_bf16(const void*, const void*, const void*, void*, void*
   return KTA_ERR_UNSUPPORTED;
 }
 
-size_t kta_decode_workspace_bytes(int64_t, int64_t, int64_t, int64_t, int64_t) { return 0; }
-
-int kta_decode_gqa_bf16(const void*, const void*, const void*, const void*, const void*, void*,
-                        int64_t, int64_t, int64_t, int64_t, int64_t, float, void*, size_t,
-                        void*) {
-  return KTA_ERR_UNSUPPORTED;
-}
-
 }  // extern "C"

@@ -62,7 +62,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kta_decode_workspace_bytes": (_size, [_i64, _i64, _i64, _i64, _i64]),
     "kta_decode_gqa_bf16": (
         ctypes.c_int,
-        [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _f32, _ptr, _size, _ptr],
+        [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _ptr, _size,
+         _ptr],
     ),
     "kta_so_gemm_bf16": (None, [_u64, _u64, _u64, _i32, _i32, _i32]),
     "kta_so_gemm_f16": (None, [_u64, _u64, _u64, _i32, _i32, _i32]),

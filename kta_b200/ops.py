@@ -154,5 +154,6 @@ def decode_gqa(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         raise ValueError(f"workspace needs {need} bytes")
     lib.call("kta_decode_gqa_bf16", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
              seqlens.data_ptr(), kv_offsets.data_ptr(), out.data_ptr(), bsz, hq, hkv, d,
-             int(max_seqlen), float(scale), workspace.data_ptr(), workspace.numel(), _stream())
+             k_cache.shape[0], int(max_seqlen), float(scale), workspace.data_ptr(),
+             workspace.numel(), _stream())
     return out
