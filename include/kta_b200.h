@@ -113,6 +113,25 @@ int kta_decode_gqa_bf16(const void* Q, const void* Kc, const void* Vc, const voi
                         int64_t D, int64_t cache_tokens, int64_t max_seqlen, float scale,
                         void* workspace, size_t ws_bytes, void* stream);
 
+/* Allocation-free kta_decode_gqa_bf16. This entry has no counterpart in the reference.
+ * Same arguments and results, minus the workspace: the partials and arrival counters live
+ * in a fixed 8 MiB array of device memory owned by the library (every GPU that loads the
+ * library holds it until the process exits). It is for callers that hand the library only
+ * their own input and output buffers and may not allocate device memory themselves: a
+ * kernel-case harness that allocates exactly the tensors a case declares and times one
+ * launch (an allocation there would synchronise the device inside the timed region), or a
+ * host whose device memory belongs to another allocator or was planned up front. Limits:
+ * calls whose workspace (kta_decode_workspace_bytes) exceeds 8 MiB return
+ * KTA_ERR_UNSUPPORTED; the entry clears the array's counters on `stream` before each launch;
+ * all calls share the one array, so calls that overlap on the GPU (other streams or host
+ * threads) race and must be serialised by the caller. The first call on a device resolves
+ * the array's device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture. */
+int kta_decode_gqa_bf16_noalloc(const void* Q, const void* Kc, const void* Vc,
+                                const void* seqlens, const void* kv_offsets, void* O, int64_t B,
+                                int64_t Hq, int64_t Hkv, int64_t D, int64_t cache_tokens,
+                                int64_t max_seqlen, float scale, void* stream);
+
 /* --- Reference-compatible `so` shims -----------------------------------------------------
  * The exact signature src/kta/measure/bench.py:80-98 calls: pointers as uint64 device
  * addresses, shape scalars as int32, restype None, default stream, the caller synchronises.

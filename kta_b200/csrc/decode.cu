@@ -24,6 +24,7 @@
 //     device (status KTA_ERR_DEVICE_BOUNDS) and that sequence's output is zero-filled.
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "kta_common.cuh"
 #include "kta_host.h"
@@ -636,6 +637,68 @@ int launch(const void* Q, const void* Kc, const void* Vc, const void* seqlens,
   return launch_status();
 }
 
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant: the workspace is a fixed array in device memory that belongs to
+// the library, so a caller that may not allocate device memory passes only its own inputs
+// and outputs. Every GPU that loads the library holds this array until the process exits.
+// ---------------------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocDevice {
+  std::once_flag once;
+  void* ptr = nullptr;  // device address of g_noalloc_scratch on this device
+  int status = KTA_OK;
+};
+NoAllocDevice g_noalloc_devices[64];
+
+// Device address of the scratch array on the current device. The host-side name of the
+// array is only a stand-in: the address comes from cudaGetSymbolAddress, resolved once per
+// device with that device current (the first allocation-free call on a device does it).
+void* noalloc_scratch(int* status) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    (void)cudaGetLastError();
+    *status = KTA_ERR_NO_DEVICE;
+    return nullptr;
+  }
+  NoAllocDevice& d = g_noalloc_devices[dev];
+  std::call_once(d.once, [&d]() {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();
+      d.status = KTA_ERR_CUDA;
+    } else {
+      d.ptr = p;
+    }
+  });
+  *status = d.status;
+  return d.ptr;
+}
+
+int launch_noalloc(const void* Q, const void* Kc, const void* Vc, const void* seqlens,
+                   const void* kv_offsets, void* O, int64_t B, int64_t Hq, int64_t Hkv,
+                   int64_t Dm, int64_t cache_tokens, int64_t max_seqlen, float scale,
+                   cudaStream_t stream) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0) return KTA_ERR_INVALID_ARG;
+  if (Hq / Hkv > MAX_GROUP || B > MAX_BATCH) return KTA_ERR_UNSUPPORTED;
+  // The partials and arrival counters this call needs must fit in the fixed array.
+  if (workspace_bytes(B, Hq, Hkv) > kNoAllocScratchBytes) return KTA_ERR_UNSUPPORTED;
+  int s = KTA_OK;
+  void* scratch = noalloc_scratch(&s);
+  if (scratch == nullptr) return s;
+  // The array keeps whatever the previous call left; the arrival counters must start at
+  // zero, so clear them on the caller's stream ahead of the kernel.
+  const size_t counters_bytes = ((static_cast<size_t>(B * Hkv) * 4 + 255) / 256) * 256;
+  if (cudaMemsetAsync(scratch, 0, counters_bytes, stream) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return KTA_ERR_CUDA;
+  }
+  return launch(Q, Kc, Vc, seqlens, kv_offsets, O, B, Hq, Hkv, Dm, cache_tokens, max_seqlen,
+                scale, scratch, kNoAllocScratchBytes, stream);
+}
+
 }  // namespace decode
 }  // namespace kta
 
@@ -656,6 +719,15 @@ int kta_decode_gqa_bf16(const void* Q, const void* Kc, const void* Vc, const voi
   return kta::decode::launch(Q, Kc, Vc, seqlens, kv_offsets, O, B, Hq, Hkv, D, cache_tokens,
                              max_seqlen, scale, workspace, ws_bytes,
                              static_cast<cudaStream_t>(stream));
+}
+
+int kta_decode_gqa_bf16_noalloc(const void* Q, const void* Kc, const void* Vc,
+                                const void* seqlens, const void* kv_offsets, void* O, int64_t B,
+                                int64_t Hq, int64_t Hkv, int64_t D, int64_t cache_tokens,
+                                int64_t max_seqlen, float scale, void* stream) {
+  return kta::decode::launch_noalloc(Q, Kc, Vc, seqlens, kv_offsets, O, B, Hq, Hkv, D,
+                                     cache_tokens, max_seqlen, scale,
+                                     static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -65,6 +65,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _ptr, _size,
          _ptr],
     ),
+    "kta_decode_gqa_bf16_noalloc": (
+        ctypes.c_int,
+        [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _ptr],
+    ),
     "kta_so_gemm_bf16": (None, [_u64, _u64, _u64, _i32, _i32, _i32]),
     "kta_so_gemm_f16": (None, [_u64, _u64, _u64, _i32, _i32, _i32]),
     "kta_so_gemm_nn_f16": (None, [_u64, _u64, _u64, _i32, _i32, _i32]),
