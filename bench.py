@@ -50,39 +50,52 @@ CPU_BUDGET_S = 12.0  # CPU baseline sample: about this much host compute
 # distributed plumbing
 # ---------------------------------------------------------------------------------------
 class Dist:
-    def __init__(self, want: int) -> None:
+    """One process per GPU: rank / world from torchrun's environment, a process group over
+    NCCL (gloo when no GPU is present: the host-side logic is tested that way), max and sum
+    reductions of per-rank scalars outside the timed region."""
+
+    def __init__(self, want: int, backend: str | None = None) -> None:
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         if want > 1 and self.world != want:
             raise SystemExit(f"--gpus {want} needs torchrun with {want} ranks (WORLD_SIZE="
                              f"{self.world})")
+        self.backend = backend or ("nccl" if torch.cuda.is_available() else "gloo")
         self.pg = None
 
     def init(self) -> None:
         if self.world > 1:
             import datetime
 
+            kw = {}
+            if self.backend == "nccl":
+                kw["device_id"] = torch.device("cuda", self.local)
             torch.distributed.init_process_group(
-                "nccl", timeout=datetime.timedelta(seconds=120),
-                device_id=torch.device("cuda", self.local))
+                self.backend, timeout=datetime.timedelta(seconds=120), **kw)
             self.pg = True
+
+    def _dev(self) -> str:
+        return "cuda" if self.backend == "nccl" else "cpu"
 
     def barrier(self) -> None:
         if self.pg:
-            torch.distributed.barrier(device_ids=[self.local])
+            if self.backend == "nccl":
+                torch.distributed.barrier(device_ids=[self.local])
+            else:
+                torch.distributed.barrier()
 
     def max(self, x: float) -> float:
         if not self.pg:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        t = torch.tensor([x], dtype=torch.float64, device=self._dev())
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
     def sum(self, x: float) -> float:
         if not self.pg:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        t = torch.tensor([x], dtype=torch.float64, device=self._dev())
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
         return float(t.item())
 

@@ -205,3 +205,47 @@ def quantize_blockwise_e4m3(x: np.ndarray, block_rows: int, block_cols: int = 12
     q = q.reshape(rb * block_rows, cb * block_cols)[:rows, :cols]
     codes = torch.from_numpy(np.ascontiguousarray(q)).to(torch.float8_e4m3fn)
     return codes.view(torch.uint8).numpy().copy(), scale
+
+
+# ---- whole input sets of a case -----------------------------------------------------------
+
+def case_inputs(problem, shape: dict[str, Any], dist: str, rng: random.Random,
+                table: dict[str, Generator] | None = None
+                ) -> tuple[dict[str, Any], dict[str, np.ndarray]]:
+    """One input set of ``problem`` at ``shape`` from the stream ``rng``: the shape with any
+    derived sizes filled in, and the host arrays in input order.
+
+    Two Problem params extend the per-tensor draw (src/kta/measure/jobs.py:120-123):
+    ``lengths`` {low, high, seqlens, offsets, total} draws per-sequence lengths uniform in
+    [low, high] (clipped to max_seqlen), packs them back to back and sets the total as a
+    shape variable; ``quantize`` {tensor: {scale, block}} draws the tensor's source values
+    from ``dist`` and stores e4m3 codes plus fp32 block scales amax/448."""
+    shape = dict(shape)
+    out: dict[str, np.ndarray] = {}
+    lengths = problem.params.get("lengths")
+    if lengths:
+        g = np.random.default_rng(rng.getrandbits(63))
+        hi = min(int(lengths["high"]), int(shape.get("max_seqlen", lengths["high"])))
+        lo = min(int(lengths["low"]), hi)
+        ln = g.integers(lo, hi + 1, size=int(shape["B"])).astype(np.int32)
+        off = np.concatenate([[0], np.cumsum(ln, dtype=np.int64)[:-1]]).astype(np.int64)
+        shape[lengths["total"]] = int(ln.sum())
+        out[lengths["seqlens"]] = ln
+        out[lengths["offsets"]] = off
+    quant = problem.params.get("quantize") or {}
+    scale_of = {v["scale"]: k for k, v in quant.items()}
+    for t in problem.inputs:
+        if t.name in out:
+            continue
+        if t.name in quant:
+            spec = TensorSpec(name=t.name, shape=t.shape, dtype="f32", layout=t.layout)
+            src = generate(spec, shape, dist, rng, table).astype(np.float32)
+            rows = int(quant[t.name]["block"][0])
+            codes, scales = quantize_blockwise_e4m3(src, rows, int(quant[t.name]["block"][1]))
+            out[t.name] = codes
+            out[quant[t.name]["scale"]] = scales
+        elif t.name in scale_of:
+            continue  # produced with its tensor
+        else:
+            out[t.name] = generate(t, shape, dist, rng, table)
+    return shape, {t.name: out[t.name] for t in problem.inputs}

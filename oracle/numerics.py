@@ -68,5 +68,5 @@ def f64_to_e4m3_bits(x: np.ndarray) -> np.ndarray:
     pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & ((idx & 1) == 0))
     code = np.where(pick_hi, idx, idx - 1)
     code = np.where(a == 0, 0, code).astype(np.uint8)
-    sign = np.where(np.signbit(x) & (code != 0), np.uint8(0x80), np.uint8(0))
+    sign = np.where(np.signbit(x), np.uint8(0x80), np.uint8(0))
     return (code | sign).astype(np.uint8)

@@ -1,0 +1,114 @@
+"""The oracle pinned against the reference's own outputs (tests/golden, made by
+tests/golden/make_golden.py from the reference's code) and against exact definitions.
+
+CPU only."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle import fp8 as ofp8
+from oracle import gemm as ogemm
+from oracle import numerics
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def st():
+    return np.load(GOLDEN / "statements.npz")
+
+
+def test_gemm_nn_matches_reference_statement_runner(st):
+    """The seed cases' `C = A @ B` through the reference's ref_torch.py (FP64)."""
+    a, b = st["nn.A"], st["nn.B"]
+    ref = st["nn.C.f64"].reshape(a.shape[0], b.shape[1])
+    np.testing.assert_allclose(ogemm.gemm_nn(a.astype(np.float64), b.astype(np.float64)), ref,
+                               rtol=1e-12, atol=1e-12)
+
+
+def test_gemm_tn_matches_reference_statement_runner(st):
+    a, b = st["nn.A"], st["tn.B"]
+    ref = st["tn.C.f64"].reshape(a.shape[0], b.shape[0])
+    np.testing.assert_allclose(ogemm.gemm_tn(a.astype(np.float64), b.astype(np.float64)), ref,
+                               rtol=1e-12, atol=1e-12)
+    # the library run in the inputs' own dtype (f16) rounds to f16: within f16 rounding
+    lib = st["tn.C.lib"].reshape(ref.shape)
+    assert np.abs(lib - ref).max() <= 2e-3 * max(1.0, np.abs(ref).max())
+
+
+def test_causal_attention_matches_reference_statement_runner(st):
+    q, k, v = st["attn.Q"], st["attn.K"], st["attn.V"]
+    bsz, s, h, d = q.shape
+    o, lse = oatt.causal_fwd(q, k, v, d ** -0.5)
+    np.testing.assert_allclose(o, st["attn.O.f64"].reshape(o.shape), rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(lse, st["attn.LSE.f64"].reshape(lse.shape), rtol=1e-10,
+                               atol=1e-12)
+
+
+def test_decode_matches_reference_statement_runner(st):
+    q, kc, vc = st["dec.Q"], st["dec.Kc"], st["dec.Vc"]
+    o = oatt.decode_gqa(q, kc, vc, st["dec.seqlens"], st["dec.offsets"], q.shape[-1] ** -0.5)
+    np.testing.assert_allclose(o, st["dec.O.f64"].reshape(o.shape), rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("chunk", [1, 4, 16, 1000])
+def test_decode_split_combine_equals_closed_form(st, chunk):
+    """The reference's split-KV partials (log2 LSE) + exp2 combine is the same function."""
+    args = (st["dec.Q"], st["dec.Kc"], st["dec.Vc"], st["dec.seqlens"], st["dec.offsets"],
+            st["dec.Q"].shape[-1] ** -0.5)
+    np.testing.assert_allclose(oatt.decode_split(*args, chunk=chunk), oatt.decode_gqa(*args),
+                               rtol=1e-12, atol=1e-12)
+
+
+def test_fp8_statement_matches_reference_statement_runner(st):
+    """The block-scaled statement, run by the reference's runner on dequantisable values."""
+    a, b, sa, sb = st["fp8.A"], st["fp8.B"], st["fp8.sa"], st["fp8.sb"]
+    ad = a.astype(np.float64) * np.repeat(sa.astype(np.float64), 128, axis=1)[:, :a.shape[1]]
+    s = np.repeat(np.repeat(sb.astype(np.float64), 128, 0), 128, 1)[:b.shape[0], :b.shape[1]]
+    ref = st["fp8.C.f64"].reshape(a.shape[0], b.shape[0])
+    np.testing.assert_allclose(ad @ (b.astype(np.float64) * s).T, ref, rtol=1e-12, atol=1e-12)
+
+
+def test_e4m3_table_matches_torch_float8():
+    codes = torch.arange(256, dtype=torch.uint8)
+    t = codes.view(torch.float8_e4m3fn).to(torch.float64).numpy()
+    ours = numerics.E4M3_TABLE
+    same = (ours == t) | (np.isnan(ours) & np.isnan(t))
+    assert same.all()
+
+
+def test_e4m3_rounding_matches_torch_cast():
+    g = np.random.default_rng(0)
+    x = np.concatenate([g.standard_normal(20000) * 50, g.uniform(-448, 448, 20000),
+                        np.array([0.0, -0.0, 448.0, -448.0, 2.0 ** -9, 2.0 ** -10, 1e-6])])
+    x = x.astype(np.float32).astype(np.float64)
+    ours = numerics.f64_to_e4m3_bits(x)
+    theirs = torch.from_numpy(x.astype(np.float32)).to(torch.float8_e4m3fn).view(torch.uint8)
+    assert np.array_equal(ours, theirs.numpy())
+
+
+def test_fp8_quantiser_matches_product_quantiser():
+    from kta_b200 import inputs as kinp
+
+    g = np.random.default_rng(1)
+    x = g.standard_normal((130, 300)) * np.where(g.random((130, 300)) < 0.01, 20, 1)
+    for rows in (1, 128):
+        c1, s1 = ofp8.quantize(x, rows)
+        c2, s2 = kinp.quantize_blockwise_e4m3(x, rows)
+        assert np.array_equal(s1, s2) and np.array_equal(c1, c2)
+
+
+def test_bf16_widening_and_rounding_match_torch():
+    g = np.random.default_rng(2)
+    x = np.concatenate([g.standard_normal(50000) * 10, np.array([0.0, 1e-40, -3.0e38])])
+    bits = numerics.f64_to_bf16_bits(x)
+    t = torch.from_numpy(x.astype(np.float32)).to(torch.bfloat16).view(torch.int16).numpy()
+    assert np.array_equal(bits.view(np.int16), t)
+    back = numerics.bf16_bits_to_f64(bits)
+    assert np.array_equal(back, torch.from_numpy(t).view(torch.bfloat16).double().numpy())
