@@ -448,6 +448,110 @@ class DecodeWorkload:
         return self.b
 
 
+class AttnWorkload:
+    """Causal attention forward, B=8 H=32 S=4096 D=128 bf16; this rank's batch x head
+    slice (the heads are independent)."""
+
+    kernel_regex = "attn_fwd_kernel"
+    unit = "TFLOP/s"
+    dtype_name = "bf16"
+    case = "attn_causal"
+    graph_default = False
+
+    def __init__(self, dist: Dist, b: int = 8, h: int = 32, s: int = 4096, d: int = 128) -> None:
+        self.b_total, self.h, self.s, self.d = b, h, s, d
+        pairs = b * h
+        lo, hi = shard(pairs, dist.world, dist.rank)
+        # whole batches when the split allows it, otherwise heads of one batch entry
+        self.pairs = hi - lo
+        if self.pairs % h == 0:
+            self.b, self.hh = self.pairs // h, h
+        else:
+            self.b, self.hh = 1, self.pairs
+
+    @property
+    def flops(self) -> float:
+        return 4.0 * self.b * self.hh * self.d * self.s * (self.s + 1) / 2
+
+    @property
+    def bytes(self) -> float:
+        return float(4 * self.b * self.s * self.hh * self.d * 2 + self.b * self.hh * self.s * 4)
+
+    def work(self) -> float:
+        return self.flops
+
+    def sol_shape(self) -> dict:
+        return {"B": self.b, "S": self.s, "H": self.hh, "D": self.d}
+
+    @property
+    def m(self) -> int:
+        return self.b * self.hh
+
+    def config(self, world: int) -> dict:
+        return {"workload": f"attn_causal: B={self.b_total} H={self.h} S={self.s} D={self.d}, "
+                            "bf16, causal, O bf16 + LSE fp32",
+                "case": self.case, "B": self.b_total, "H": self.h, "S": self.s, "D": self.d,
+                "global_batch": self.b_total, "seq_len": self.s,
+                "parallelism": f"batch x head shards x{world} (no collective)",
+                "l2": "inputs larger than L2: 4 rotating Q/K/V sets (1.07 GB each), no flush",
+                "inputs": "N(0,1) bf16 from a seeded torch generator"}
+
+    def setup(self, device: torch.device) -> None:
+        g = torch.Generator(device=device).manual_seed(77)
+        shp = (self.b, self.s, self.hh, self.d)
+        self.qkv = [[_randn(shp, torch.bfloat16, g) for _ in range(3)] for _ in range(NSETS)]
+        self.o = [torch.empty(shp, dtype=torch.bfloat16, device=device) for _ in range(NSETS)]
+        self.lse = [torch.empty((self.b, self.hh, self.s), dtype=torch.float32, device=device)
+                    for _ in range(NSETS)]
+
+    def launch(self, i: int) -> None:
+        from kta_b200 import ops
+
+        j = i % NSETS
+        q, k, v = self.qkv[j]
+        ops.attn_fwd_causal(q, k, v, out=self.o[j], lse=self.lse[j])
+
+    def setup_e2e(self, device: torch.device) -> None:
+        g = torch.Generator().manual_seed(99)
+        shp = (self.b, self.s, self.hh, self.d)
+        self.hqkv = [_randn(shp, torch.bfloat16, g, device="cpu").pin_memory() for _ in range(3)]
+        self.ho = torch.empty(shp, dtype=torch.bfloat16).pin_memory()
+        self.hl = torch.empty((self.b, self.hh, self.s), dtype=torch.float32).pin_memory()
+        self.dqkv = [torch.empty_like(t, device=device) for t in self.hqkv]
+        self.do = torch.empty_like(self.ho, device=device)
+        self.dl = torch.empty_like(self.hl, device=device)
+        self.h2d_bytes = 3 * self.hqkv[0].numel() * 2
+        self.d2h_bytes = self.ho.numel() * 2 + self.hl.numel() * 4
+
+    def e2e_step(self) -> None:
+        from kta_b200 import ops
+
+        for d, h in zip(self.dqkv, self.hqkv):
+            d.copy_(h, non_blocking=True)
+        ops.attn_fwd_causal(*self.dqkv, out=self.do, lse=self.dl)
+        self.ho.copy_(self.do, non_blocking=True)
+        self.hl.copy_(self.dl, non_blocking=True)
+
+    def cpu_sample(self, pairs: int):
+        """The case statement in bf16 on the host for `pairs` (batch, head) pairs."""
+        pairs = max(1, min(pairs, self.b * self.hh))
+        g = torch.Generator().manual_seed(7)
+        shp = (1, self.s, pairs, self.d)
+        q, k, v = (_randn(shp, torch.bfloat16, g, device="cpu") for _ in range(3))
+
+        def run():
+            from kta_b200 import schemas
+            from oracle import statement
+
+            stmt = schemas.load_case_file("attn_causal").problem.reference_impl
+            statement.run_library(stmt, {"Q": q, "K": k, "V": v},
+                                  {"B": 1, "S": self.s, "H": pairs, "D": self.d}, ["O", "LSE"])
+
+        units = 4.0 * pairs * self.d * self.s * (self.s + 1) / 2
+        return run, units, (f"causal attention statement in bf16 on the host for {pairs} of "
+                            f"{self.b * self.hh} (batch, head) pairs, S={self.s}")
+
+
 WORKLOADS = {
     "gemm_bf16_8192": lambda d: GemmWorkload("gemm_bf16_8192", 8192, 8192, 8192,
                                              torch.bfloat16, d, "gemm_bf16_8192"),
@@ -456,6 +560,7 @@ WORKLOADS = {
     "gemm_f16_1024": lambda d: GemmWorkload("gemm_f16_1024", 1024, 1024, 1024,
                                             torch.float16, d, "gemm_f16_1024"),
     "decode_gqa": lambda d: DecodeWorkload(d),
+    "attn_causal": lambda d: AttnWorkload(d),
 }
 
 

@@ -9,9 +9,4 @@ int kta_gemm_fp8_blockscaled(const void*, const void*, const void*, const void*,
   return KTA_ERR_UNSUPPORTED;
 }
 
-int kta_attn_fwd_causal_bf16(const void*, const void*, const void*, void*, void*, int64_t,
-                             int64_t, int64_t, int64_t, float, void*) {
-  return KTA_ERR_UNSUPPORTED;
-}
-
 }  // extern "C"
