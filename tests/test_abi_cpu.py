@@ -86,12 +86,20 @@ def test_noalloc_decode_refuses_what_does_not_fit_its_array():
     assert L.kta_decode_gqa_bf16_noalloc(*args, 0, 32, 8, 128, 1024, 64, 0.1, None) == 1
 
 
-@pytest.mark.skip(reason="attention and FP8 entries still reject every call")
-def test_attention_and_fp8_argument_checks():
+def test_attention_argument_checks():
     L = lib.load()
     a = [ALIGNED] * 5
     assert L.kta_attn_fwd_causal_bf16(*a, 2, 4, 256, 64, 0.1, None) == 2      # D != 128
     assert L.kta_attn_fwd_causal_bf16(None, *a[1:], 2, 4, 256, 128, 0.1, None) == 1
+    assert L.kta_attn_fwd_causal_bf16(*a, 2, 4, 0, 128, 0.1, None) == 1       # S = 0
+    assert L.kta_attn_fwd_causal_bf16(*a, 2, 4, 256, 128, 0.0, None) == 1     # scale
+    assert L.kta_attn_fwd_causal_bf16(MISALIGNED, *a[1:], 2, 4, 256, 128, 0.1, None) == 3
+
+
+@pytest.mark.skip(reason="the FP8 entry still rejects every call")
+def test_fp8_argument_checks():
+    L = lib.load()
+    a = [ALIGNED] * 5
     assert L.kta_gemm_fp8_blockscaled(*a, 128, 128, 100, None) in (1, 2, 3)    # K % 16
     assert L.kta_gemm_fp8_blockscaled(None, *a[1:], 128, 128, 128, None) == 1
 
