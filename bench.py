@@ -552,6 +552,119 @@ class AttnWorkload:
                             f"{self.b * self.hh} (batch, head) pairs, S={self.s}")
 
 
+class Fp8Workload:
+    """FP8 e4m3 block-scaled GEMM M=4096 N=7168 K=7168 (bf16 out); this rank's N-column
+    shard, aligned to the 128-wide weight-scale blocks."""
+
+    kernel_regex = "fp8_gemm_kernel"
+    unit = "TFLOP/s"
+    dtype_name = "e4m3"
+    case = "gemm_fp8_blockscaled"
+    graph_default = False
+    peak_key = "fp8"
+
+    def __init__(self, dist: Dist, m: int = 4096, n: int = 7168, k: int = 7168) -> None:
+        self.m, self.n_total, self.k = m, n, k
+        lo, hi = shard(n, dist.world, dist.rank, align=128)
+        self.n0, self.n = lo, hi - lo
+
+    @property
+    def flops(self) -> float:
+        return 2.0 * self.m * self.n * self.k
+
+    @property
+    def bytes(self) -> float:
+        kb = -(-self.k // 128)
+        return float(self.m * self.k + self.n * self.k + self.m * self.n * 2
+                     + 4 * (self.m * kb + -(-self.n // 128) * kb))
+
+    def work(self) -> float:
+        return self.flops
+
+    def sol_shape(self) -> dict:
+        return {"M": self.m, "N": self.n, "K": self.k}
+
+    def config(self, world: int) -> dict:
+        return {"workload": f"gemm_fp8_blockscaled: M={self.m} N={self.n_total} K={self.k}, "
+                            "e4m3 with fp32 scales per 1x128 (A) and 128x128 (B), bf16 out",
+                "case": self.case, "M": self.m, "N": self.n_total, "K": self.k,
+                "global_batch": self.m, "seq_len": None,
+                "parallelism": f"N-column shards x{world} (no collective)",
+                "l2": "inputs larger than L2: 4 rotating input sets (~88 MB each)",
+                "inputs": "N(0,1) with 1% outliers x20, quantised on the device"}
+
+    def _quant(self, x: torch.Tensor, rows: int):
+        m, k = x.shape
+        xb = x.view(m // rows if rows > 1 else m, rows, k // 128, 128) if rows > 1 else \
+            x.view(m, 1, k // 128, 128)
+        amax = xb.abs().amax(dim=(1, 3)).clamp_min(1e-30)
+        scale = (amax / 448.0).float()
+        q = (xb / scale[:, None, :, None]).view(m, k).to(torch.float8_e4m3fn)
+        return q, scale.contiguous()
+
+    def setup(self, device: torch.device) -> None:
+        g = torch.Generator(device=device).manual_seed(55)
+        self.sets = []
+        for _ in range(NSETS):
+            a = torch.randn(self.m, self.k, generator=g, device=device)
+            a = torch.where(torch.rand(a.shape, generator=g, device=device) < 0.01, a * 20, a)
+            b = torch.randn(self.n, self.k, generator=g, device=device)
+            b = torch.where(torch.rand(b.shape, generator=g, device=device) < 0.01, b * 20, b)
+            qa, sa = self._quant(a, 1)
+            qb, sb = self._quant(b, 128)
+            del a, b
+            self.sets.append((qa, sa, qb, sb))
+        self.c = [torch.empty((self.m, self.n), dtype=torch.bfloat16, device=device)
+                  for _ in range(NSETS)]
+
+    def launch(self, i: int) -> None:
+        from kta_b200 import ops
+
+        j = i % NSETS
+        ops.gemm_fp8_blockscaled(*self.sets[j], out=self.c[j])
+
+    def setup_e2e(self, device: torch.device) -> None:
+        qa, sa, qb, sb = self.sets[0]
+        self.h = [t.cpu().pin_memory() for t in (qa.view(torch.uint8), sa, qb.view(torch.uint8), sb)]
+        self.dv = [torch.empty_like(t, device=device) for t in self.h]
+        self.hc = torch.empty((self.m, self.n), dtype=torch.bfloat16).pin_memory()
+        self.dc = torch.empty_like(self.hc, device=device)
+        self.h2d_bytes = sum(t.numel() * t.element_size() for t in self.h)
+        self.d2h_bytes = self.hc.numel() * 2
+
+    def e2e_step(self) -> None:
+        from kta_b200 import ops
+
+        for d, h in zip(self.dv, self.h):
+            d.copy_(h, non_blocking=True)
+        ops.gemm_fp8_blockscaled(self.dv[0].view(torch.float8_e4m3fn), self.dv[1],
+                                 self.dv[2].view(torch.float8_e4m3fn), self.dv[3], out=self.dc)
+        self.hc.copy_(self.dc, non_blocking=True)
+
+    def cpu_sample(self, rows: int):
+        """The case statement (dequantise, then multiply) in fp32 on the host for `rows` rows
+        of A: the inputs' own precision there is fp32 scales and e4m3 codes widened."""
+        rows = max(1, min(rows, self.m))
+        g = torch.Generator().manual_seed(7)
+        a = torch.randn(rows, self.k, generator=g).to(torch.float8_e4m3fn).float()
+        b = torch.randn(self.n_total, self.k, generator=g).to(torch.float8_e4m3fn).float()
+        kb = -(-self.k // 128)
+        sa = torch.rand(rows, kb, generator=g) + 0.5
+        sb = torch.rand(-(-self.n_total // 128), kb, generator=g) + 0.5
+
+        def run():
+            from kta_b200 import schemas
+            from oracle import statement
+
+            stmt = schemas.load_case_file("gemm_fp8_blockscaled").problem.reference_impl
+            statement.run_library(stmt, {"A": a, "sa": sa, "B": b, "sb": sb},
+                                  {"M": rows, "N": self.n_total, "K": self.k}, ["C"])
+
+        units = 2.0 * rows * self.n_total * self.k
+        return run, units, (f"dequantise-and-multiply statement in fp32 on the host, M={rows} "
+                            f"rows (of {self.m}), N={self.n_total}, K={self.k}")
+
+
 WORKLOADS = {
     "gemm_bf16_8192": lambda d: GemmWorkload("gemm_bf16_8192", 8192, 8192, 8192,
                                              torch.bfloat16, d, "gemm_bf16_8192"),
@@ -561,6 +674,7 @@ WORKLOADS = {
                                             torch.float16, d, "gemm_f16_1024"),
     "decode_gqa": lambda d: DecodeWorkload(d),
     "attn_causal": lambda d: AttnWorkload(d),
+    "gemm_fp8": lambda d: Fp8Workload(d),
 }
 
 

@@ -96,12 +96,13 @@ def test_attention_argument_checks():
     assert L.kta_attn_fwd_causal_bf16(MISALIGNED, *a[1:], 2, 4, 256, 128, 0.1, None) == 3
 
 
-@pytest.mark.skip(reason="the FP8 entry still rejects every call")
 def test_fp8_argument_checks():
     L = lib.load()
     a = [ALIGNED] * 5
-    assert L.kta_gemm_fp8_blockscaled(*a, 128, 128, 100, None) in (1, 2, 3)    # K % 16
+    assert L.kta_gemm_fp8_blockscaled(*a, 128, 128, 100, None) == 3    # K % 16
+    assert L.kta_gemm_fp8_blockscaled(*a, 128, 100, 128, None) == 3    # N % 8
     assert L.kta_gemm_fp8_blockscaled(None, *a[1:], 128, 128, 128, None) == 1
+    assert L.kta_gemm_fp8_blockscaled(*a, 0, 128, 128, None) == 1
 
 
 def test_so_shim_reports_through_last_error():
