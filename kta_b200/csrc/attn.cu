@@ -10,10 +10,10 @@
 //     walks the units head-major (the query tiles of one head run at the same time on
 //     different SMs, so that head's K and V come from HBM once and then from L2), heaviest
 //     pair first, in a snake order that balances the causal triangle;
-//   * warp 0: TMA producer (4-D maps over [B, S, H, D], 128-byte swizzle; Q_A/Q_B once per
-//     unit, K/V tiles through a 2-stage ring); warp 1: TMEM owner and the single-thread MMA
-//     issuer; warps 2-5 and 6-9: the softmax warpgroups of tiles A and B (thread = query row =
-//     TMEM lane);
+//   * warp 0: TMA producer of Q (once per unit) and K (3-stage ring), warp 10: of V (2-stage
+//     ring), all through 4-D maps over [B, S, H, D] with 128-byte swizzle; warp 1: TMEM owner
+//     and the single-thread MMA issuer; warps 2-5 and 6-9: the softmax warpgroups of tiles A
+//     and B (thread = query row = TMEM lane);
 //   * TMEM: S_A, S_B (128 columns each), O_A, O_B (128 each). P (bf16) is written back over
 //     the first 64 columns of its S and read by O += P V straight from TMEM (A operand in
 //     tensor memory, V as an MN-major shared-memory operand): no shared-memory round trip;
@@ -37,8 +37,10 @@ namespace attn {
 constexpr int D = 128;
 constexpr int BM = 128;                 // query rows per tile
 constexpr int BN = 128;                 // KV rows per tile
-constexpr int NUM_THREADS = 320;        // producer, MMA, two softmax warpgroups
-constexpr int KV_STAGES = 2;
+constexpr int NUM_THREADS = 352;        // K/Q producer, MMA, two softmax warpgroups, V producer
+constexpr int K_STAGES = 3;
+constexpr int V_STAGES = 2;
+constexpr int V_PRODUCER_WARP = 10;
 constexpr int HALF = 128 * 64 * 2;      // [128 rows][64 d] bf16, one swizzle column
 constexpr int TILE = 2 * HALF;          // [128 rows][128 d]
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: rescale when the max grew > 2^8
@@ -62,11 +64,11 @@ enum : unsigned int {
 struct Layout {
   static constexpr int OFF_Q = 0;                           // Q_A, Q_B
   static constexpr int OFF_K = OFF_Q + 2 * TILE;
-  static constexpr int OFF_V = OFF_K + KV_STAGES * TILE;
-  static constexpr int OFF_BAR = OFF_V + KV_STAGES * TILE;
-  // q_full, q_empty, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], o_done[2],
-  // o_free[2]
-  static constexpr int NUM_BARS = 2 + 3 * KV_STAGES + 8;
+  static constexpr int OFF_V = OFF_K + K_STAGES * TILE;
+  static constexpr int OFF_BAR = OFF_V + V_STAGES * TILE;
+  // q_full, q_empty, k_full[K], k_empty[K], v_full[V], v_empty[V], s_full[2], p_full[2],
+  // o_done[2], o_free[2]
+  static constexpr int NUM_BARS = 2 + 2 * K_STAGES + 2 * V_STAGES + 8;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int TOTAL = OFF_MISC + 16;
   static constexpr int ALLOC = TOTAL + 1024;
@@ -135,6 +137,73 @@ __device__ __forceinline__ int snake(int k, int c, int g) {
   return k * g + ((k & 1) ? (g - 1 - c) : c);
 }
 
+// One softmax step for this thread's query row over a 128-column S tile in TMEM: the row
+// maximum (pass 1), the decision to move the running maximum, and P = 2^(s*scale - m) packed
+// to bf16 pairs over the S columns already consumed (pass 2). DIAG applies the causal mask
+// (key c visible to query `row` iff c <= row); off the diagonal no mask code runs.
+template <bool DIAG>
+__device__ __forceinline__ void softmax_tile(uint32_t t_s, int row, float sl, float& m_used,
+                                             float& factor, bool& rescale, float& rowsum) {
+  float mx[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+    uint32_t r0[32], r1[32];
+    tmem_ld_32x32b_x32(t_s + c, r0);
+    tmem_ld_32x32b_x32(t_s + c + 32, r1);
+    tmem_ld_wait();
+    reg_fence(r0);
+    reg_fence(r1);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float v0 = __uint_as_float(r0[i]), v1 = __uint_as_float(r1[i]);
+      if (DIAG) {
+        v0 = (c + i <= row) ? v0 : -INFINITY;
+        v1 = (c + 32 + i <= row) ? v1 : -INFINITY;
+      }
+      mx[i & 7] = fmaxf(mx[i & 7], fmaxf(v0, v1));
+    }
+  }
+  const float rmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl;
+  if (rmax > m_used + RESCALE_THRESHOLD) {
+    factor = ex2(m_used - rmax);  // 0 on the first tile (m_used = -inf)
+    rescale = m_used != -INFINITY;
+    m_used = rmax;
+  }
+  const float neg = -m_used;
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+    uint32_t r0[32], r1[32];
+    tmem_ld_32x32b_x32(t_s + c, r0);
+    tmem_ld_32x32b_x32(t_s + c + 32, r1);
+    tmem_ld_wait();
+    reg_fence(r0);
+    reg_fence(r1);
+    uint32_t pk[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float v0 = __uint_as_float(r0[2 * i]), v1 = __uint_as_float(r0[2 * i + 1]);
+      float w0 = __uint_as_float(r1[2 * i]), w1 = __uint_as_float(r1[2 * i + 1]);
+      if (DIAG) {
+        v0 = (c + 2 * i <= row) ? v0 : -INFINITY;
+        v1 = (c + 2 * i + 1 <= row) ? v1 : -INFINITY;
+        w0 = (c + 32 + 2 * i <= row) ? w0 : -INFINITY;
+        w1 = (c + 32 + 2 * i + 1 <= row) ? w1 : -INFINITY;
+      }
+      const float e0 = ex2(fmaf(v0, sl, neg)), e1 = ex2(fmaf(v1, sl, neg));
+      const float f0 = ex2(fmaf(w0, sl, neg)), f1 = ex2(fmaf(w1, sl, neg));
+      sum[i & 3] += (e0 + e1) + (f0 + f1);
+      pk[i] = pack_bf16x2(e0, e1);
+      pk[16 + i] = pack_bf16x2(f0, f1);
+    }
+    tmem_st_32x32b_x32(t_s + c / 2, pk);
+  }
+  rowsum = (sum[0] + sum[1]) + (sum[2] + sum[3]);
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -144,9 +213,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
   uint64_t* k_full = bars + 2;
-  uint64_t* v_full = k_full + KV_STAGES;
-  uint64_t* kv_empty = v_full + KV_STAGES;
-  uint64_t* s_full = kv_empty + KV_STAGES;  // [tile]
+  uint64_t* k_empty = k_full + K_STAGES;
+  uint64_t* v_full = k_empty + K_STAGES;
+  uint64_t* v_empty = v_full + V_STAGES;
+  uint64_t* s_full = v_empty + V_STAGES;    // [tile]
   uint64_t* p_full = s_full + 2;            // [tile]
   uint64_t* o_done = p_full + 2;            // [tile]: the unit's last PV completed
   uint64_t* o_free = o_done + 2;            // [tile]: the epilogue read O
@@ -158,10 +228,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int s = 0; s < KV_STAGES; ++s) {
+    for (int s = 0; s < K_STAGES; ++s) {
       mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < V_STAGES; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -188,40 +261,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int num_units = p.batch * p.heads * p.pairs;
   const int rounds = (num_units + gridDim.x - 1) / gridDim.x;
 
-  if (warp == 0) {
-    // ------------------------------ TMA producer ------------------------------
+  if (warp == 0 || warp == V_PRODUCER_WARP) {
+    // ------------------- TMA producers: Q and K (warp 0), V (warp 10) -------------------
     if (lane == 0) {
+      const bool is_k = warp == 0;
       uint32_t kv_t = 0, qphase = 0;
       bool ok = true;
       for (int k = 0; k < rounds && ok; ++k) {
         const int u = snake(k, blockIdx.x, gridDim.x);
         if (u >= num_units) continue;
         const Unit un = unit_of(u, p);
-        if (!mbar_wait(q_empty, qphase ^ 1u, abort_flag, p.status, SITE_PROD_Q)) break;
-        qphase ^= 1u;
-        const int q0 = 2 * un.pair * BM;
-        mbar_arrive_expect_tx(q_full, un.has_b ? 2 * TILE : TILE);
-        tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q, 0, un.h, q0, un.b);
-        tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + HALF, 64, un.h, q0, un.b);
-        if (un.has_b) {
-          tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE, 0, un.h, q0 + BM, un.b);
-          tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE + HALF, 64, un.h, q0 + BM, un.b);
+        if (is_k) {
+          if (!mbar_wait(q_empty, qphase ^ 1u, abort_flag, p.status, SITE_PROD_Q)) break;
+          qphase ^= 1u;
+          const int q0 = 2 * un.pair * BM;
+          mbar_arrive_expect_tx(q_full, un.has_b ? 2 * TILE : TILE);
+          tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q, 0, un.h, q0, un.b);
+          tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + HALF, 64, un.h, q0, un.b);
+          if (un.has_b) {
+            tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE, 0, un.h, q0 + BM, un.b);
+            tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE + HALF, 64, un.h, q0 + BM,
+                        un.b);
+          }
         }
+        const int nst = is_k ? K_STAGES : V_STAGES;
+        uint64_t* fullb = is_k ? k_full : v_full;
+        uint64_t* emptyb = is_k ? k_empty : v_empty;
+        const CUtensorMap* map = is_k ? &tmK : &tmV;
+        uint8_t* base = smem + (is_k ? Layout::OFF_K : Layout::OFF_V);
         for (int j = 0; j < un.nkv; ++j, ++kv_t) {
-          const int st = static_cast<int>(kv_t % KV_STAGES);
-          const uint32_t ph = (kv_t / KV_STAGES) & 1u;
-          if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, SITE_PROD_KV)) {
+          const int st = static_cast<int>(kv_t % nst);
+          const uint32_t ph = (kv_t / nst) & 1u;
+          if (!mbar_wait(&emptyb[st], ph ^ 1u, abort_flag, p.status, SITE_PROD_KV)) {
             ok = false;
             break;
           }
-          uint8_t* kb = smem + Layout::OFF_K + st * TILE;
-          uint8_t* vb = smem + Layout::OFF_V + st * TILE;
-          mbar_arrive_expect_tx(&k_full[st], TILE);
-          tma_load_4d(&tmK, &k_full[st], kb, 0, un.h, j * BN, un.b);
-          tma_load_4d(&tmK, &k_full[st], kb + HALF, 64, un.h, j * BN, un.b);
-          mbar_arrive_expect_tx(&v_full[st], TILE);
-          tma_load_4d(&tmV, &v_full[st], vb, 0, un.h, j * BN, un.b);
-          tma_load_4d(&tmV, &v_full[st], vb + HALF, 64, un.h, j * BN, un.b);
+          uint8_t* dst = base + st * TILE;
+          mbar_arrive_expect_tx(&fullb[st], TILE);
+          tma_load_4d(map, &fullb[st], dst, 0, un.h, j * BN, un.b);
+          tma_load_4d(map, &fullb[st], dst + HALF, 64, un.h, j * BN, un.b);
         }
       }
     }
@@ -280,15 +358,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int a_last = 2 * un.pair;  // tile A's diagonal KV tile
         uint32_t prev_v = 0;
         for (int j = 0; j < un.nkv && ok; ++j, ++kv_t) {
-          const int st = static_cast<int>(kv_t % KV_STAGES);
-          const uint32_t ph = (kv_t / KV_STAGES) & 1u;
-          if (!mbar_wait(&k_full[st], ph, abort_flag, p.status, SITE_MMA_K)) {
+          const int ks = static_cast<int>(kv_t % K_STAGES);
+          const int vs = static_cast<int>(kv_t % V_STAGES);
+          if (!mbar_wait(&k_full[ks], (kv_t / K_STAGES) & 1u, abort_flag, p.status,
+                         SITE_MMA_K)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t kaddr = smem_u32(smem + Layout::OFF_K + st * TILE);
-          const uint32_t vaddr = smem_u32(smem + Layout::OFF_V + st * TILE);
+          const uint32_t kaddr = smem_u32(smem + Layout::OFF_K + ks * TILE);
+          const uint32_t vaddr = smem_u32(smem + Layout::OFF_V + vs * TILE);
           const bool a_on = j <= a_last;
           if (a_on) issue_s(0, kaddr);
           if (un.has_b && j > 0) {
@@ -296,10 +375,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               ok = false;
               break;
             }
+            // V(j-1) is free once PV_B(j-1) (and everything before it) completed
+            umma_commit(&v_empty[(kv_t - 1) % V_STAGES]);
           }
           if (un.has_b) issue_s(1, kaddr);
+          umma_commit(&k_empty[ks]);  // both reads of K(j) issued
           if (j == un.nkv - 1) umma_commit(q_empty);  // the unit's last reads of Q issued
-          if (!mbar_wait(&v_full[st], ph, abort_flag, p.status, SITE_MMA_V)) {
+          if (!mbar_wait(&v_full[vs], (kv_t / V_STAGES) & 1u, abort_flag, p.status,
+                         SITE_MMA_V)) {
             ok = false;
             break;
           }
@@ -311,19 +394,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             if (j == a_last) umma_commit(&o_done[0]);
           }
-          if (!un.has_b) {
-            umma_commit(&kv_empty[st]);
-          } else if (j > 0) {
-            // the previous tile's V is free once PV_B(j-1) (and everything before) is done
-            umma_commit(&kv_empty[(kv_t - 1) % KV_STAGES]);
-          }
+          if (!un.has_b) umma_commit(&v_empty[vs]);
           prev_v = vaddr;
         }
         if (!ok) break;
         if (un.has_b) {
           if (!issue_pv(1, prev_v, un.nkv - 1 == 0)) break;
           umma_commit(&o_done[1]);
-          umma_commit(&kv_empty[(kv_t - 1) % KV_STAGES]);
+          umma_commit(&v_empty[(kv_t - 1) % V_STAGES]);
         } else {
           umma_commit(&o_done[1]);  // tile B absent: its epilogue only hands O_B back
         }
@@ -357,64 +435,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           sphase ^= 1u;
           tc_fence_after();
-          const bool diag = (j == qt);  // key c is visible to query `row` iff c <= row
-          // pass 1: row maximum of the raw scores, 32 columns at a time
-          float mx[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-#pragma unroll
-          for (int c = 0; c < BN; c += 32) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(t_s + c, r);
-            tmem_ld_wait();
-            reg_fence(r);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float v = (!diag || c + i <= row) ? __uint_as_float(r[i]) : -INFINITY;
-              mx[i & 7] = fmaxf(mx[i & 7], v);
-            }
-          }
-          const float rmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl;
-          float factor = 1.f;
+          float factor = 1.f, rowsum = 0.f;
           bool rescale = false;
-          if (rmax > m_used + RESCALE_THRESHOLD) {
-            factor = ex2(m_used - rmax);  // 0 on the first tile (m_used = -inf)
-            rescale = m_used != -INFINITY;
-            m_used = rmax;
+          if (j == qt) {
+            softmax_tile<true>(t_s, row, sl, m_used, factor, rescale, rowsum);
+          } else {
+            softmax_tile<false>(t_s, row, sl, m_used, factor, rescale, rowsum);
           }
-          const float neg = -m_used;
-          // pass 2: P = 2^(s*scale - m), 64 columns at a time, packed bf16 pairs written over
-          // the S columns already consumed
-          float sum[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 64) {
-            uint32_t r0[32], r1[32];
-            tmem_ld_32x32b_x32(t_s + c, r0);
-            tmem_ld_32x32b_x32(t_s + c + 32, r1);
-            tmem_ld_wait();
-            reg_fence(r0);
-            reg_fence(r1);
-            uint32_t pk[32];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float v0 = __uint_as_float(r0[2 * i]), v1 = __uint_as_float(r0[2 * i + 1]);
-              float w0 = __uint_as_float(r1[2 * i]), w1 = __uint_as_float(r1[2 * i + 1]);
-              if (diag) {
-                v0 = (c + 2 * i <= row) ? v0 : -INFINITY;
-                v1 = (c + 2 * i + 1 <= row) ? v1 : -INFINITY;
-                w0 = (c + 32 + 2 * i <= row) ? w0 : -INFINITY;
-                w1 = (c + 32 + 2 * i + 1 <= row) ? w1 : -INFINITY;
-              }
-              const float e0 = ex2(fmaf(v0, sl, neg)), e1 = ex2(fmaf(v1, sl, neg));
-              const float f0 = ex2(fmaf(w0, sl, neg)), f1 = ex2(fmaf(w1, sl, neg));
-              sum[i & 3] += (e0 + e1) + (f0 + f1);
-              pk[i] = pack_bf16x2(e0, e1);
-              pk[16 + i] = pack_bf16x2(f0, f1);
-            }
-            tmem_st_32x32b_x32(t_s + c / 2, pk);
-          }
-          lsum = lsum * factor + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+          lsum = lsum * factor + rowsum;
           if (__any_sync(0xffffffffu, rescale)) {
             // PV(j-1) of this tile completed before S(j) did (same issuing thread)
             const float f = rescale ? factor : 1.f;
