@@ -283,10 +283,9 @@ class GemmWorkload:
     def e2e_step(self) -> None:
         from kta_b200 import ops
 
-        self.da.copy_(self.ha, non_blocking=True)
-        self.db.copy_(self.hb, non_blocking=True)
-        ops.gemm(self.da, self.db, out=self.dc)
-        self.hc.copy_(self.dc, non_blocking=True)
+        # the public host-buffer entry: B, then A in row blocks copied in, each block's GEMM
+        # as soon as it landed, C blocks copied out behind it (copies overlap compute)
+        ops.gemm_host(self.ha, self.hb, out=self.hc)
 
     # ---- the reference's CPU torch path on a bounded sample ----
     def cpu_sample(self, rows: int):

@@ -19,6 +19,7 @@
 // along K over a thread-block cluster whose partial sums are reduced through distributed
 // shared memory, so every SM streams B and no global workspace is needed.
 #include <algorithm>
+#include <cstdlib>
 
 #include "kta_common.cuh"
 #include "kta_host.h"
@@ -272,6 +273,285 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// 2-SM variant (tn): a cluster of two CTAs computes one 256 x 256 tile with
+// tcgen05.mma.cta_group::2. Each CTA loads its own 128 rows of A and 128 rows of B per
+// stage (no multicast); the leader (cluster rank 0) issues the MMAs, which read A and B
+// from both CTAs' shared memory, and each CTA's TMEM receives its 128 rows x 256 columns.
+// Per SM the tensor core reads 8 KB of operands per 256x256x16 step instead of 12 KB
+// for the 1-SM 128x256 tile, and L2 serves a third less operand traffic per FLOP.
+// ---------------------------------------------------------------------------------------
+constexpr int P_STAGES = 6;
+constexpr int P_BM = 256;   // rows of A per CTA pair (128 per CTA)
+constexpr int P_BN = 256;   // rows of B per CTA pair (128 per CTA)
+
+struct PairLayout {
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = 128 * BK * 2;
+  static constexpr int C_BYTES = 32 * EPI_COLS * 2;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + P_STAGES * A_BYTES;
+  static constexpr int OFF_C = OFF_B + P_STAGES * B_BYTES;
+  static constexpr int OFF_BAR = OFF_C + EPI_WARPS * 2 * C_BYTES;
+  static constexpr int NUM_BARS = 2 * P_STAGES + 4;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int TOTAL = OFF_MISC + 16;
+  static constexpr int ALLOC = TOTAL + 1024;
+  static_assert(ALLOC <= 232448, "shared memory budget of one sm_100 CTA");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank_u32() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory object in cluster rank `rank` (shared::cluster window).
+__device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void pair_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on the leader's
+// barrier (`bar_cluster` is a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster,
+                                                 void* dst, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      " .reg .pred p;\n"
+      " setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the barrier at this offset in both CTAs of the pair when every tcgen05
+// op issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n"
+      " .reg .b16 m;\n"
+      " mov.b16 m, 3;\n"
+      " tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], m;\n"
+      "}\n" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
+                     unsigned int* status) {
+  using L = PairLayout;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);  // leader's counts both CTAs
+  uint64_t* empty = full + P_STAGES;                                 // in each CTA
+  uint64_t* tfull = empty + P_STAGES;                                // in each CTA
+  uint64_t* tempty = tfull + 2;                                      // leader's counts both
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = warp_id();
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank_u32();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 2 * EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  pair_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int tiles_m = (M + P_BM - 1) / P_BM;
+  const int tiles_n = (N + P_BN - 1) / P_BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
+        int mb, nb;
+        tile_coords(tile, tiles_m, tiles_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, SITE_PRODUCER_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar0 = peer_addr(&full[stage], 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (L::A_BYTES + L::B_BYTES));
+          tma_load_2d_pair(&tmA, bar0, smem + L::OFF_A + stage * L::A_BYTES, kb * BK,
+                           mb * P_BM + static_cast<int>(rank) * 128);
+          tma_load_2d_pair(&tmB, bar0, smem + L::OFF_B + stage * L::B_BYTES, kb * BK,
+                           nb * P_BN + static_cast<int>(rank) * 128);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (leader && lane == 0) {
+      constexpr uint32_t fmt = BF16 ? 1u : 0u;
+      constexpr uint32_t idesc = make_idesc(P_BM, P_BN, fmt, fmt, 0u, 0u);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, status, SITE_MMA_TEMPTY)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * P_BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, status, SITE_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + L::OFF_A + stage * L::A_BYTES);
+          const uint32_t b0 = smem_u32(smem + L::OFF_B + stage * L::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            umma_f16_pair(d_tmem, sdesc_sw128(a0 + k * UMMA_K * 2, 16, 1024),
+                          sdesc_sw128(b0 + k * UMMA_K * 2, 16, 1024), idesc,
+                          (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage]);  // frees this stage in both CTAs
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc]);  // each CTA's half of the accumulator is complete
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows x 256 columns ----------------
+    const int q = warp & 3;
+    uint8_t* cbuf = smem + L::OFF_C + (warp - 2) * 2 * L::C_BYTES;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int buf = 0;
+    const uint32_t tempty0[2] = {peer_addr(&tempty[0], 0), peer_addr(&tempty[1], 0)};
+    for (int tile = pair; tile < num_tiles; tile += pairs) {
+      int mb, nb;
+      tile_coords(tile, tiles_m, tiles_n, mb, nb);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, status, SITE_EPI_TFULL)) break;
+      tc_fence_after();
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * P_BN);
+      const int row0 = mb * P_BM + static_cast<int>(rank) * 128 + q * 32;
+#pragma unroll 1
+      for (int c = 0; c < P_BN / EPI_COLS; ++c) {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(t_row + c * EPI_COLS, r0);
+        tmem_ld_32x32b_x32(t_row + c * EPI_COLS + 32, r1);
+        tmem_ld_wait();
+        reg_fence(r0);
+        reg_fence(r1);
+        if (c == P_BN / EPI_COLS - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty0[acc]);
+        }
+        uint32_t pk[32];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          pk[j] = pack2<BF16>(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1]));
+          pk[16 + j] = pack2<BF16>(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1]));
+        }
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        uint8_t* sbuf = cbuf + buf * L::C_BYTES;
+        const uint32_t rowa = smem_u32(sbuf) + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          st_shared_v4(rowa + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4), pk[4 * j],
+                       pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, sbuf, nb * P_BN + c * EPI_COLS, row0);
+          bulk_commit_group();
+        }
+        buf ^= 1;
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  pair_sync();  // the leader's MMAs into this CTA's TMEM and remote arrivals are over
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512)
+                 : "memory");
   }
 }
 
@@ -589,6 +869,59 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
   return launch_status();
 }
 
+template <bool BF16>
+int launch_pair(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda,
+                int64_t ldb, int64_t ldc, cudaStream_t stream) {
+  using L = PairLayout;
+  const CUtensorMapDataType dt =
+      BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb, tc;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+    const uint32_t box[2] = {BK, 128};
+    int s = encode_tmap(&ta, dt, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t box[2] = {BK, 128};
+    int s = encode_tmap(&tb, dt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldc) * 2};
+    const uint32_t box[2] = {EPI_COLS, 32};
+    int s = encode_tmap(&tc, dt, 2, C, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  }
+  auto kernel = gemm_pair_kernel<BF16>;
+  int s = set_smem(kernel, L::ALLOC);
+  if (s != KTA_OK) return s;
+  const int tiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+  const int pairs = std::max(1, std::min(tiles, current_sm_count() / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = L::ALLOC;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, M, N, K, device_status_ptr());
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return KTA_ERR_LAUNCH;
+  }
+  return launch_status();
+}
+
 // Estimated relative time of a tile width: waves x columns, discounted by how close the
 // tile runs to the shared-memory bandwidth limit (128x64 tiles feed the tensor core at
 // 192 B/clk against 128 B/clk available; 128x128 at 128; 128x256 at 96).
@@ -597,6 +930,16 @@ inline double tile_cost(int M, int N, int BN, int sms) {
   const long tiles = static_cast<long>((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const long waves = (tiles + sms - 1) / sms;
   return static_cast<double>(waves) * BN / eff;
+}
+
+// Selection of the 2-SM path: KTA_GEMM_PAIR=0 never, =force always (tn, M >= 129),
+// unset: when its 256x256 tiles fill the machine about as well as 128x256 ones.
+inline int pair_mode() {
+  const char* v = std::getenv("KTA_GEMM_PAIR");
+  if (v == nullptr) return 1;
+  if (v[0] == '0') return 0;
+  if (v[0] == 'f') return 2;
+  return 1;
 }
 
 template <bool BF16, bool B_KMAJOR>
@@ -619,6 +962,20 @@ int dispatch(const void* A, const void* B, void* C, int64_t M64, int64_t N64, in
     return launch_skinny<64, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
   }
   const int sms = std::max(1, current_sm_count());
+  const int mode = B_KMAJOR ? pair_mode() : 0;
+  if (mode == 2 && M > 128 && sms >= 2) {
+    return launch_pair<BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+  }
+  if (mode == 1 && sms >= 2) {
+    // 2-SM 256x256 tiles when they fill the machine about as well as 128x256 ones
+    const long pair_tiles = static_cast<long>((M + 255) / 256) * ((N + 255) / 256);
+    const long pair_waves = (pair_tiles + sms / 2 - 1) / (sms / 2);
+    const long one_tiles = static_cast<long>((M + 127) / 128) * ((N + 255) / 256);
+    const long one_waves = (one_tiles + sms - 1) / sms;
+    if (pair_tiles >= sms / 2 && pair_waves <= one_waves) {
+      return launch_pair<BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+    }
+  }
   const double c256 = tile_cost(M, N, 256, sms);
   const double c128 = tile_cost(M, N, 128, sms);
   const double c64 = tile_cost(M, N, 64, sms);

@@ -157,3 +157,72 @@ def decode_gqa(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
              k_cache.shape[0], int(max_seqlen), float(scale), workspace.data_ptr(),
              workspace.numel(), _stream())
     return out
+
+
+class _HostPipe:
+    """Device buffers and streams of one host-buffer GEMM shape, kept across calls."""
+
+    def __init__(self, m: int, n: int, k: int, dtype: torch.dtype, device: torch.device) -> None:
+        self.a = torch.empty((m, k), dtype=dtype, device=device)
+        self.b = torch.empty((n, k), dtype=dtype, device=device)
+        self.c = torch.empty((m, n), dtype=dtype, device=device)
+        self.h2d = torch.cuda.Stream(device=device)
+        self.comp = torch.cuda.Stream(device=device)
+        self.d2h = torch.cuda.Stream(device=device)
+
+
+_PIPES: dict[tuple, _HostPipe] = {}
+
+
+def gemm_host(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+              chunks: int = 8, device: torch.device | None = None) -> torch.Tensor:
+    """C = A @ B.T with A, B and C in (pinned) host memory, end to end.
+
+    The call copies B to the device, then A in ``chunks`` row blocks; each block's GEMM
+    starts as soon as its rows have landed, and each block of C is copied back as soon as it
+    is computed, on three streams, so host-device traffic in both directions overlaps the
+    tensor-core work. Returns once C is complete on the host. Device buffers are kept per
+    shape between calls."""
+    if a.is_cuda or b.is_cuda:
+        raise ValueError("gemm_host takes host tensors")
+    m, k = a.shape
+    n, kb = b.shape
+    if kb != k or a.dtype != b.dtype:
+        raise ValueError("A [M, K] and B [N, K] of one dtype")
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    key = (m, n, k, a.dtype, device)
+    pipe = _PIPES.get(key)
+    if pipe is None:
+        pipe = _PIPES[key] = _HostPipe(m, n, k, a.dtype, device)
+    if out is None:
+        out = torch.empty((m, n), dtype=a.dtype, pin_memory=True)
+    caller = torch.cuda.current_stream(device)
+    chunks = max(1, min(chunks, -(-m // 128)))
+    rows = -(-m // chunks)
+    rows = -(-rows // 128) * 128
+    pipe.h2d.wait_stream(caller)
+    with torch.cuda.stream(pipe.h2d):
+        pipe.b.copy_(b, non_blocking=True)
+        b_ready = torch.cuda.Event()
+        b_ready.record(pipe.h2d)
+        a_ready = []
+        for r0 in range(0, m, rows):
+            pipe.a[r0:r0 + rows].copy_(a[r0:r0 + rows], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(pipe.h2d)
+            a_ready.append(ev)
+    c_ready = []
+    with torch.cuda.stream(pipe.comp):
+        pipe.comp.wait_event(b_ready)
+        for i, r0 in enumerate(range(0, m, rows)):
+            pipe.comp.wait_event(a_ready[i])
+            gemm(pipe.a[r0:r0 + rows], pipe.b, out=pipe.c[r0:r0 + rows])
+            ev = torch.cuda.Event()
+            ev.record(pipe.comp)
+            c_ready.append(ev)
+    with torch.cuda.stream(pipe.d2h):
+        for i, r0 in enumerate(range(0, m, rows)):
+            pipe.d2h.wait_event(c_ready[i])
+            out[r0:r0 + rows].copy_(pipe.c[r0:r0 + rows], non_blocking=True)
+    caller.wait_stream(pipe.d2h)
+    return out

@@ -121,3 +121,17 @@ def test_device_status_clean_after_gemms(cuda_device):
     from kta_b200 import lib
 
     assert lib.device_status(clear=True)[0] == 0
+
+
+@pytest.mark.parametrize("m,n,k,chunks", [(1000, 520, 256, 3), (4096, 2048, 1024, 8),
+                                          (100, 64, 64, 8)])
+def test_gemm_host_buffers_pipelined(cuda_device, m, n, k, chunks):
+    """The host-buffer entry: pinned A, B in, pinned C out, copies overlapped with the GEMM
+    row blocks on three streams."""
+    from kta_b200 import ops
+
+    a, b = _inputs(m, n, k, torch.bfloat16)
+    c = ops.gemm_host(a.pin_memory(), b.pin_memory(), chunks=chunks)
+    torch.cuda.synchronize()
+    assert not c.is_cuda
+    _check(c, ogemm.gemm_tn(a.double().numpy(), b.double().numpy()))
