@@ -10,20 +10,29 @@
 //     walks the units head-major (the query tiles of one head run at the same time on
 //     different SMs, so that head's K and V come from HBM once and then from L2), heaviest
 //     pair first, in a snake order that balances the causal triangle;
-//   * warp 0: TMA producer of Q (once per unit) and K (3-stage ring), warp 10: of V (2-stage
-//     ring), all through 4-D maps over [B, S, H, D] with 128-byte swizzle; warp 1: TMEM owner
-//     and the single-thread MMA issuer; warps 2-5 and 6-9: the softmax warpgroups of tiles A
-//     and B (thread = query row = TMEM lane);
+//   * three warpgroups: warps 0-3 and 4-7 are the softmax warpgroups of tiles A and B
+//     (thread = query row = TMEM lane); in the third, warp 8 is the TMA producer of Q (once
+//     per unit) and K (3-stage ring), warp 9 the TMEM owner and MMA issuer (the warp walks
+//     the schedule, one elected lane issues), warp 10 the TMA producer of V (2-stage ring),
+//     warp 11 idle; all loads go through 4-D
+//     maps over [B, S, H, D] with 128-byte swizzle. setmaxnreg moves registers from the
+//     third warpgroup (88 per thread) to the softmax ones (208), which hold a whole S row;
 //   * TMEM: S_A, S_B (128 columns each), O_A, O_B (128 each). P (bf16) is written back over
 //     the first 64 columns of its S and read by O += P V straight from TMEM (A operand in
 //     tensor memory, V as an MN-major shared-memory operand): no shared-memory round trip;
 //   * MMA order per KV tile j: S_A(j), PV_B(j-1), S_B(j), PV_A(j): while one warpgroup turns
 //     S into P the tensor core works for the other; tcgen05 ops of one thread complete in
-//     order, so "S(j) done" also means "PV(j-1) done" for the same tile;
-//   * softmax without per-element branches: max on raw scores, one FFMA (scale, subtract)
-//     and one ex2.approx.ftz per element; the running maximum moves only when the true one
-//     grew by more than 2^8, so O and the row sum are corrected rarely (the final division by
-//     the row sum is exact either way); the causal mask is applied on diagonal tiles only;
+//     order, so "S(j) done" also means "PV(j-1) done" for the same tile. The softmax
+//     publishes P in two halves (keys 0-63, 64-127) and PV starts on the first while the
+//     second is computed;
+//   * softmax in one pass over a row held in registers: max on raw scores (3-input max),
+//     packed f32x2 FFMA for scale-and-subtract, and the exponentials split between the MUFU
+//     (ex2.approx.ftz) and the FMA pipe (Cody-Waite reduction 2^x = 2^j 2^f, |f| <= 1/2, with
+//     a degree-3 minimax polynomial for 2^f, max relative error 7.5e-5, far below bf16's
+//     rounding of P); the running maximum moves only when the true one grew by more than
+//     2^8, so O and the row sum are corrected rarely (the final division by the row sum is
+//     exact either way); the causal mask is applied on diagonal tiles only, whose
+//     exponentials all go to the MUFU (it maps -inf to 0);
 //   * every mbarrier wait is bounded.
 #include <algorithm>
 #include <cmath>
@@ -37,10 +46,16 @@ namespace attn {
 constexpr int D = 128;
 constexpr int BM = 128;                 // query rows per tile
 constexpr int BN = 128;                 // KV rows per tile
-constexpr int NUM_THREADS = 352;        // K/Q producer, MMA, two softmax warpgroups, V producer
+constexpr int NUM_THREADS = 384;        // two softmax warpgroups, producers + MMA warpgroup
 constexpr int K_STAGES = 3;
 constexpr int V_STAGES = 2;
+constexpr int QK_PRODUCER_WARP = 8;
+constexpr int MMA_WARP = 9;
 constexpr int V_PRODUCER_WARP = 10;
+constexpr int SOFTMAX_REGS = 208;       // 2 x 128 x 208 + 128 x 88 = 384 x 168 (launch)
+constexpr int OTHER_REGS = 88;
+// exponentials evaluated on the FMA pipe, per 8 column pairs of an off-diagonal tile
+constexpr int EXP_POLY_PER_8 = 3;
 constexpr int HALF = 128 * 64 * 2;      // [128 rows][64 d] bf16, one swizzle column
 constexpr int TILE = 2 * HALF;          // [128 rows][128 d]
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: rescale when the max grew > 2^8
@@ -66,9 +81,9 @@ struct Layout {
   static constexpr int OFF_K = OFF_Q + 2 * TILE;
   static constexpr int OFF_V = OFF_K + K_STAGES * TILE;
   static constexpr int OFF_BAR = OFF_V + V_STAGES * TILE;
-  // q_full, q_empty, k_full[K], k_empty[K], v_full[V], v_empty[V], s_full[2], p_full[2],
-  // o_done[2], o_free[2]
-  static constexpr int NUM_BARS = 2 + 2 * K_STAGES + 2 * V_STAGES + 8;
+  // q_full, q_empty, k_full[K], k_empty[K], v_full[V], v_empty[V], s_full[2],
+  // p_full[2][2] (tile, half of P), o_done[2], o_free[2]
+  static constexpr int NUM_BARS = 2 + 2 * K_STAGES + 2 * V_STAGES + 10;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int TOTAL = OFF_MISC + 16;
   static constexpr int ALLOC = TOTAL + 1024;
@@ -94,10 +109,84 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n"
+      " .reg .pred P;\n"
+      " elect.sync _|P, 0xffffffff;\n"
+      " selp.b32 %0, 1, 0, P;\n"
+      "}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// packed pairs of fp32 (sm_100 f32x2 arithmetic: one instruction, two lanes of work)
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x0, 2^x1 on the FMA pipe for x <= 2^8 (the rescale threshold bounds x from above).
+// Cody-Waite: j = round(x) by the 1.5 * 2^23 shifter, f = x - j in [-1/2, 1/2], 2^f from a
+// degree-3 polynomial (minimax in relative error, fitted for this kernel: max 7.5e-5), and
+// 2^j added into the exponent field. x is clamped at -125 so that 2^j p(f) stays a normal
+// number; 2^-125 stands in for smaller results (they vanish against a row sum >= 1).
+__device__ __forceinline__ void exp2_poly_pair(uint64_t x, float& e0, float& e1) {
+  float x0, x1;
+  f2_split(x, x0, x1);
+  x = f2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t shifter = f2(12582912.f, 12582912.f);
+  const uint64_t unshift = f2(-12582912.f, -12582912.f);
+  const uint64_t t = add2(x, shifter);             // low mantissa bits hold j
+  const uint64_t fr = sub2(x, add2(t, unshift));
+  uint64_t p = fma2(f2(0.0551716648f, 0.0551716648f), fr, f2(0.242611170f, 0.242611170f));
+  p = fma2(p, fr, f2(0.693260968f, 0.693260968f));
+  p = fma2(p, fr, f2(0.999928057f, 0.999928057f));
+  float p0, p1, t0, t1;
+  f2_split(p, p0, p1);
+  f2_split(t, t0, t1);
+  e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -141,67 +230,91 @@ __device__ __forceinline__ int snake(int k, int c, int g) {
 // maximum (pass 1), the decision to move the running maximum, and P = 2^(s*scale - m) packed
 // to bf16 pairs over the S columns already consumed (pass 2). DIAG applies the causal mask
 // (key c visible to query `row` iff c <= row); off the diagonal no mask code runs.
+// One S tile of one query row (this thread's TMEM lane): P = 2^(S sl - m) as bf16 over the
+// first 64 columns, published in two halves (p_half[0], p_half[1]), the running maximum m
+// (log2 units) and the row sum l. When m moved, O is rescaled in TMEM before the first half
+// is published (PV(j-1) completed before S(j) did: same issuing thread, in order).
 template <bool DIAG>
-__device__ __forceinline__ void softmax_tile(uint32_t t_s, int row, float sl, float& m_used,
-                                             float& factor, bool& rescale, float& rowsum) {
+__device__ __forceinline__ void softmax_step(uint32_t t_s, uint32_t t_o, int row, int lane,
+                                             float sl, float& m_used, float& lsum,
+                                             uint64_t* p_half) {
+  uint32_t r[BN];
+#pragma unroll
+  for (int q = 0; q < BN / 32; ++q) {
+    tmem_ld_32x32b_x32(t_s + q * 32, *reinterpret_cast<uint32_t(*)[32]>(r + q * 32));
+  }
+  tmem_ld_wait();
+  reg_fence(r);
+  if (DIAG) {
+#pragma unroll
+    for (int c = 0; c < BN; ++c) {
+      if (c > row) r[c] = __float_as_uint(-INFINITY);
+    }
+  }
   float mx[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 64) {
-    uint32_t r0[32], r1[32];
-    tmem_ld_32x32b_x32(t_s + c, r0);
-    tmem_ld_32x32b_x32(t_s + c + 32, r1);
-    tmem_ld_wait();
-    reg_fence(r0);
-    reg_fence(r1);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float v0 = __uint_as_float(r0[i]), v1 = __uint_as_float(r1[i]);
-      if (DIAG) {
-        v0 = (c + i <= row) ? v0 : -INFINITY;
-        v1 = (c + 32 + i <= row) ? v1 : -INFINITY;
-      }
-      mx[i & 7] = fmaxf(mx[i & 7], fmaxf(v0, v1));
-    }
+  for (int i = 0; i < BN / 2; ++i) {
+    mx[i & 7] = max3(mx[i & 7], __uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
   }
-  const float rmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl;
+  const float rmax = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]),
+                          fmaxf(mx[6], mx[7])) * sl;
+  float factor = 1.f;
+  bool rescale = false;
   if (rmax > m_used + RESCALE_THRESHOLD) {
-    factor = ex2(m_used - rmax);  // 0 on the first tile (m_used = -inf)
+    factor = ex2(m_used - rmax);  // 0 on the first tile (m_used = -inf, lsum = 0)
     rescale = m_used != -INFINITY;
     m_used = rmax;
   }
-  const float neg = -m_used;
-  float sum[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 64) {
-    uint32_t r0[32], r1[32];
-    tmem_ld_32x32b_x32(t_s + c, r0);
-    tmem_ld_32x32b_x32(t_s + c + 32, r1);
-    tmem_ld_wait();
-    reg_fence(r0);
-    reg_fence(r1);
+  lsum *= factor;
+  const bool any_rescale = __any_sync(0xffffffffu, rescale);
+  const uint64_t sl2 = f2(sl, sl);
+  const uint64_t neg2 = f2(-m_used, -m_used);
+  uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
     uint32_t pk[32];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float v0 = __uint_as_float(r0[2 * i]), v1 = __uint_as_float(r0[2 * i + 1]);
-      float w0 = __uint_as_float(r1[2 * i]), w1 = __uint_as_float(r1[2 * i + 1]);
-      if (DIAG) {
-        v0 = (c + 2 * i <= row) ? v0 : -INFINITY;
-        v1 = (c + 2 * i + 1 <= row) ? v1 : -INFINITY;
-        w0 = (c + 32 + 2 * i <= row) ? w0 : -INFINITY;
-        w1 = (c + 32 + 2 * i + 1 <= row) ? w1 : -INFINITY;
+    for (int i = 0; i < 32; ++i) {
+      const int c = h * 64 + 2 * i;
+      const uint64_t x = fma2(f2(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sl2, neg2);
+      float e0, e1;
+      if (!DIAG && (i & 7) >= 8 - EXP_POLY_PER_8) {
+        exp2_poly_pair(x, e0, e1);
+      } else {
+        float x0, x1;
+        f2_split(x, x0, x1);
+        e0 = ex2(x0);
+        e1 = ex2(x1);
       }
-      const float e0 = ex2(fmaf(v0, sl, neg)), e1 = ex2(fmaf(v1, sl, neg));
-      const float f0 = ex2(fmaf(w0, sl, neg)), f1 = ex2(fmaf(w1, sl, neg));
-      sum[i & 3] += (e0 + e1) + (f0 + f1);
+      sum2[i & 3] = add2(sum2[i & 3], f2(e0, e1));
       pk[i] = pack_bf16x2(e0, e1);
-      pk[16 + i] = pack_bf16x2(f0, f1);
     }
-    tmem_st_32x32b_x32(t_s + c / 2, pk);
+    if (h == 0 && any_rescale) {
+      // with half of the row already turned into P, fewer registers are live here
+      const float f = rescale ? factor : 1.f;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(t_o + c, o);
+        tmem_ld_wait();
+        reg_fence(o);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+        tmem_st_32x32b_x32(t_o + c, o);
+      }
+    }
+    tmem_st_32x32b_x32(t_s + h * 32, pk);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&p_half[h]);
   }
-  rowsum = (sum[0] + sum[1]) + (sum[2] + sum[3]);
+  const uint64_t s01 = add2(add2(sum2[0], sum2[1]), add2(sum2[2], sum2[3]));
+  float s0, s1;
+  f2_split(s01, s0, s1);
+  lsum += s0 + s1;
 }
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -217,8 +330,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* v_full = k_empty + K_STAGES;
   uint64_t* v_empty = v_full + V_STAGES;
   uint64_t* s_full = v_empty + V_STAGES;    // [tile]
-  uint64_t* p_full = s_full + 2;            // [tile]
-  uint64_t* o_done = p_full + 2;            // [tile]: the unit's last PV completed
+  uint64_t* p_full = s_full + 2;            // [tile][half]: P columns of keys 64h..64h+63
+  uint64_t* o_done = p_full + 4;            // [tile]: the unit's last PV completed
   uint64_t* o_free = o_done + 2;            // [tile]: the epilogue read O
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Layout::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Layout::OFF_MISC + 4);
@@ -238,19 +351,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[2 * i], 4);
+      mbar_init(&p_full[2 * i + 1], 4);
       mbar_init(&o_done[i], 1);
       mbar_init(&o_free[i], 4);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) {
+  if (warp == QK_PRODUCER_WARP && lane == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
   }
-  if (warp == 1) {
+  if (warp == MMA_WARP) {
     tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
@@ -261,81 +375,104 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int num_units = p.batch * p.heads * p.pairs;
   const int rounds = (num_units + gridDim.x - 1) / gridDim.x;
 
-  if (warp == 0 || warp == V_PRODUCER_WARP) {
-    // ------------------- TMA producers: Q and K (warp 0), V (warp 10) -------------------
-    if (lane == 0) {
-      const bool is_k = warp == 0;
-      uint32_t kv_t = 0, qphase = 0;
-      bool ok = true;
-      for (int k = 0; k < rounds && ok; ++k) {
-        const int u = snake(k, blockIdx.x, gridDim.x);
-        if (u >= num_units) continue;
-        const Unit un = unit_of(u, p);
-        if (is_k) {
-          if (!mbar_wait(q_empty, qphase ^ 1u, abort_flag, p.status, SITE_PROD_Q)) break;
-          qphase ^= 1u;
-          const int q0 = 2 * un.pair * BM;
-          mbar_arrive_expect_tx(q_full, un.has_b ? 2 * TILE : TILE);
-          tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q, 0, un.h, q0, un.b);
-          tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + HALF, 64, un.h, q0, un.b);
-          if (un.has_b) {
-            tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE, 0, un.h, q0 + BM, un.b);
-            tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE + HALF, 64, un.h, q0 + BM,
-                        un.b);
+  // registers move from the producer/MMA warpgroup to the softmax warpgroups; each
+  // setmaxnreg dominates the code of its warpgroup
+  if (warp >= QK_PRODUCER_WARP) {
+    setmaxnreg_dec<OTHER_REGS>();
+    if (warp == QK_PRODUCER_WARP || warp == V_PRODUCER_WARP) {
+      // ------------------- TMA producers: Q and K (warp 8), V (warp 10) -------------------
+      if (lane == 0) {
+        const bool is_k = warp == QK_PRODUCER_WARP;
+        uint32_t kv_t = 0, qphase = 0;
+        bool ok = true;
+        for (int k = 0; k < rounds && ok; ++k) {
+          const int u = snake(k, blockIdx.x, gridDim.x);
+          if (u >= num_units) continue;
+          const Unit un = unit_of(u, p);
+          if (is_k) {
+            if (!mbar_wait(q_empty, qphase ^ 1u, abort_flag, p.status, SITE_PROD_Q)) break;
+            qphase ^= 1u;
+            const int q0 = 2 * un.pair * BM;
+            mbar_arrive_expect_tx(q_full, un.has_b ? 2 * TILE : TILE);
+            tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q, 0, un.h, q0, un.b);
+            tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + HALF, 64, un.h, q0, un.b);
+            if (un.has_b) {
+              tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE, 0, un.h, q0 + BM, un.b);
+              tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE + HALF, 64, un.h, q0 + BM,
+                          un.b);
+            }
           }
-        }
-        const int nst = is_k ? K_STAGES : V_STAGES;
-        uint64_t* fullb = is_k ? k_full : v_full;
-        uint64_t* emptyb = is_k ? k_empty : v_empty;
-        const CUtensorMap* map = is_k ? &tmK : &tmV;
-        uint8_t* base = smem + (is_k ? Layout::OFF_K : Layout::OFF_V);
-        for (int j = 0; j < un.nkv; ++j, ++kv_t) {
-          const int st = static_cast<int>(kv_t % nst);
-          const uint32_t ph = (kv_t / nst) & 1u;
-          if (!mbar_wait(&emptyb[st], ph ^ 1u, abort_flag, p.status, SITE_PROD_KV)) {
-            ok = false;
-            break;
+          const int nst = is_k ? K_STAGES : V_STAGES;
+          uint64_t* fullb = is_k ? k_full : v_full;
+          uint64_t* emptyb = is_k ? k_empty : v_empty;
+          const CUtensorMap* map = is_k ? &tmK : &tmV;
+          uint8_t* base = smem + (is_k ? Layout::OFF_K : Layout::OFF_V);
+          for (int j = 0; j < un.nkv; ++j, ++kv_t) {
+            const int st = static_cast<int>(kv_t % nst);
+            const uint32_t ph = (kv_t / nst) & 1u;
+            if (!mbar_wait(&emptyb[st], ph ^ 1u, abort_flag, p.status, SITE_PROD_KV)) {
+              ok = false;
+              break;
+            }
+            uint8_t* dst = base + st * TILE;
+            mbar_arrive_expect_tx(&fullb[st], TILE);
+            tma_load_4d(map, &fullb[st], dst, 0, un.h, j * BN, un.b);
+            tma_load_4d(map, &fullb[st], dst + HALF, 64, un.h, j * BN, un.b);
           }
-          uint8_t* dst = base + st * TILE;
-          mbar_arrive_expect_tx(&fullb[st], TILE);
-          tma_load_4d(map, &fullb[st], dst, 0, un.h, j * BN, un.b);
-          tma_load_4d(map, &fullb[st], dst + HALF, 64, un.h, j * BN, un.b);
         }
       }
-    }
-  } else if (warp == 1) {
-    // ------------------------------ MMA issuer ------------------------------
-    if (lane == 0) {
+    } else if (warp == MMA_WARP) {
+      // ------------------------------ MMA issuer ------------------------------
+      // The whole warp walks the schedule (converged control flow: the shared-memory
+      // descriptors are warp-uniform), one elected lane issues each group of MMAs together
+      // with the commits that track it.
       constexpr uint32_t idesc_s = make_idesc(BM, BN, 1u, 1u, 0u, 0u);  // Q K^T, both K-major
       constexpr uint32_t idesc_o = make_idesc(BM, D, 1u, 1u, 0u, 1u);   // P (TMEM) V (MN-major)
-      const uint32_t qs = smem_u32(smem + Layout::OFF_Q);
+      const uint64_t qdesc = sdesc_sw128(smem_u32(smem + Layout::OFF_Q), 16, 1024);
       uint32_t kv_t = 0, qphase = 0;
       uint32_t pphase[2] = {0, 0};
       uint32_t ofree_phase[2] = {0, 0};
       int units_done = 0;
       bool ok = true;
-      auto issue_s = [&](int tile, uint32_t kaddr) {
-        const uint32_t qa = qs + tile * TILE;
+      // descriptor start addresses are in 16-byte units: stepping one adds (bytes >> 4)
+      auto issue_s = [&](int tile, uint64_t kdesc, uint64_t* extra0, uint64_t* extra1) {
+        const uint64_t adesc = qdesc + static_cast<uint64_t>((tile * TILE) >> 4);
+        if (elect_one_sync()) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_f16(tmem + t_s_col(tile), sdesc_sw128(qa + off, 16, 1024),
-                   sdesc_sw128(kaddr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = ((kk >> 2) * HALF + (kk & 3) * 32) >> 4;
+            umma_f16(tmem + t_s_col(tile), adesc + off, kdesc + off, idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[tile]);
+          if (extra0 != nullptr) umma_commit(extra0);
+          if (extra1 != nullptr) umma_commit(extra1);
         }
-        umma_commit(&s_full[tile]);
+        __syncwarp();
       };
-      auto issue_pv = [&](int tile, uint32_t vaddr, bool first) -> bool {
-        if (!mbar_wait(&p_full[tile], pphase[tile], abort_flag, p.status, SITE_MMA_P)) {
-          return false;
+      auto issue_pv = [&](int tile, uint64_t vdesc, bool first, uint64_t* done0,
+                          uint64_t* done1) -> bool {
+        // P arrives in two halves (keys 0-63, 64-127): the first half of PV starts while the
+        // softmax still works on the second
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(&p_full[2 * tile + h], pphase[tile], abort_flag, p.status,
+                         SITE_MMA_P)) {
+            return false;
+          }
+          tc_fence_after();
+          if (elect_one_sync()) {
+#pragma unroll
+            for (int kk = h * BN / 32; kk < (h + 1) * BN / 32; ++kk) {
+              umma_f16_tmem_a(tmem + t_o_col(tile), tmem + t_s_col(tile) + kk * 8,
+                              vdesc + static_cast<uint64_t>(kk * 16 * 128 / 16), idesc_o,
+                              (!first || kk > 0) ? 1u : 0u);
+            }
+            if (h == 1 && done0 != nullptr) umma_commit(done0);
+            if (h == 1 && done1 != nullptr) umma_commit(done1);
+          }
+          __syncwarp();
         }
         pphase[tile] ^= 1u;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          umma_f16_tmem_a(tmem + t_o_col(tile), tmem + t_s_col(tile) + kk * 8,
-                          sdesc_sw128(vaddr + kk * 16 * 128, HALF, 1024), idesc_o,
-                          (!first || kk > 0) ? 1u : 0u);
-        }
         return true;
       };
       for (int k = 0; k < rounds && ok; ++k) {
@@ -356,7 +493,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_after();
         const int a_last = 2 * un.pair;  // tile A's diagonal KV tile
-        uint32_t prev_v = 0;
+        uint64_t prev_vdesc = 0;
         for (int j = 0; j < un.nkv && ok; ++j, ++kv_t) {
           const int ks = static_cast<int>(kv_t % K_STAGES);
           const int vs = static_cast<int>(kv_t % V_STAGES);
@@ -366,21 +503,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t kaddr = smem_u32(smem + Layout::OFF_K + ks * TILE);
-          const uint32_t vaddr = smem_u32(smem + Layout::OFF_V + vs * TILE);
+          const uint64_t kdesc = sdesc_sw128(smem_u32(smem + Layout::OFF_K + ks * TILE), 16, 1024);
+          const uint64_t vdesc =
+              sdesc_sw128(smem_u32(smem + Layout::OFF_V + vs * TILE), HALF, 1024);
           const bool a_on = j <= a_last;
-          if (a_on) issue_s(0, kaddr);
+          // K(j) is released by the commit after its last reader; Q after the unit's last S
+          uint64_t* q_rel = j == un.nkv - 1 ? q_empty : nullptr;
+          if (a_on) issue_s(0, kdesc, un.has_b ? nullptr : &k_empty[ks], un.has_b ? nullptr : q_rel);
           if (un.has_b && j > 0) {
-            if (!issue_pv(1, prev_v, j - 1 == 0)) {
+            // V(j-1) is free once PV_B(j-1) (and everything before it) completed
+            if (!issue_pv(1, prev_vdesc, j - 1 == 0, &v_empty[(kv_t - 1) % V_STAGES], nullptr)) {
               ok = false;
               break;
             }
-            // V(j-1) is free once PV_B(j-1) (and everything before it) completed
-            umma_commit(&v_empty[(kv_t - 1) % V_STAGES]);
           }
-          if (un.has_b) issue_s(1, kaddr);
-          umma_commit(&k_empty[ks]);  // both reads of K(j) issued
-          if (j == un.nkv - 1) umma_commit(q_empty);  // the unit's last reads of Q issued
+          if (un.has_b) issue_s(1, kdesc, &k_empty[ks], q_rel);
           if (!mbar_wait(&v_full[vs], (kv_t / V_STAGES) & 1u, abort_flag, p.status,
                          SITE_MMA_V)) {
             ok = false;
@@ -388,29 +525,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after();
           if (a_on) {
-            if (!issue_pv(0, vaddr, j == 0)) {
+            if (!issue_pv(0, vdesc, j == 0, j == a_last ? &o_done[0] : nullptr,
+                          un.has_b ? nullptr : &v_empty[vs])) {
               ok = false;
               break;
             }
-            if (j == a_last) umma_commit(&o_done[0]);
           }
-          if (!un.has_b) umma_commit(&v_empty[vs]);
-          prev_v = vaddr;
+          prev_vdesc = vdesc;
         }
         if (!ok) break;
         if (un.has_b) {
-          if (!issue_pv(1, prev_v, un.nkv - 1 == 0)) break;
-          umma_commit(&o_done[1]);
-          umma_commit(&v_empty[(kv_t - 1) % V_STAGES]);
+          if (!issue_pv(1, prev_vdesc, un.nkv - 1 == 0, &o_done[1],
+                        &v_empty[(kv_t - 1) % V_STAGES])) {
+            break;
+          }
         } else {
-          umma_commit(&o_done[1]);  // tile B absent: its epilogue only hands O_B back
+          if (elect_one_sync()) umma_commit(&o_done[1]);  // tile B absent: hand O_B back
+          __syncwarp();
         }
         ++units_done;
       }
     }
   } else {
+    setmaxnreg_inc<SOFTMAX_REGS>();
     // ------------- softmax, O correction and epilogue (thread = query row) -------------
-    const int tile = (warp - 2) >> 2;        // 0: tile A (warps 2-5), 1: tile B (warps 6-9)
+    const int tile = warp >> 2;              // 0: tile A (warps 0-3), 1: tile B (warps 4-7)
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -435,32 +574,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           sphase ^= 1u;
           tc_fence_after();
-          float factor = 1.f, rowsum = 0.f;
-          bool rescale = false;
           if (j == qt) {
-            softmax_tile<true>(t_s, row, sl, m_used, factor, rescale, rowsum);
+            softmax_step<true>(t_s, t_o, row, lane, sl, m_used, lsum, &p_full[2 * tile]);
           } else {
-            softmax_tile<false>(t_s, row, sl, m_used, factor, rescale, rowsum);
+            softmax_step<false>(t_s, t_o, row, lane, sl, m_used, lsum, &p_full[2 * tile]);
           }
-          lsum = lsum * factor + rowsum;
-          if (__any_sync(0xffffffffu, rescale)) {
-            // PV(j-1) of this tile completed before S(j) did (same issuing thread)
-            const float f = rescale ? factor : 1.f;
-#pragma unroll
-            for (int c = 0; c < D; c += 32) {
-              uint32_t r[32];
-              tmem_ld_32x32b_x32(t_o + c, r);
-              tmem_ld_wait();
-              reg_fence(r);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-              tmem_st_32x32b_x32(t_o + c, r);
-            }
-          }
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&p_full[tile]);
         }
         if (!ok) break;
       }
@@ -506,7 +624,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
