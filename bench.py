@@ -677,14 +677,6 @@ WORKLOADS = {
 }
 
 
-def _extra_workloads() -> None:
-    try:
-        from kta_b200 import bench_workloads  # attention, decode, fp8 (when built)
-    except ImportError:
-        return
-    WORKLOADS.update(bench_workloads.WORKLOADS)
-
-
 # ---------------------------------------------------------------------------------------
 # measurement
 # ---------------------------------------------------------------------------------------
@@ -979,7 +971,6 @@ def run_reference(args, dist: Dist) -> dict | None:
 
 
 def main() -> int:
-    _extra_workloads()
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
