@@ -559,22 +559,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // Skinny M (<= 64): swap-AB, K split over a cluster, DSMEM reduction.
 // ---------------------------------------------------------------------------------------
 constexpr int SK_ROWS = 128;  // rows of B (columns of C) per CTA: UMMA M
-constexpr int SK_STAGES = 8;
+constexpr int SK_SUB = 2;     // 64-wide K boxes per stage: each row of B is read in 256-byte runs
+constexpr int SK_BK = SK_SUB * BK;
 constexpr int SK_THREADS = NUM_THREADS;
 
 template <int MP>
 struct SkinnyLayout {
-  static constexpr int B_BYTES = SK_ROWS * BK * 2;  // "A operand": 128 rows of B
-  static constexpr int A_BYTES = MP * BK * 2;       // "B operand": MP rows of A
-  static constexpr int STAGE_BYTES = B_BYTES + ((A_BYTES + 1023) / 1024) * 1024;
+  static constexpr int B_SUB = SK_ROWS * BK * 2;                  // one box: 128 rows of B
+  static constexpr int A_SUB = ((MP * BK * 2 + 1023) / 1024) * 1024;  // one box: MP rows of A
+  static constexpr int B_BYTES = SK_SUB * B_SUB;                  // "A operand"
+  static constexpr int A_BYTES = SK_SUB * A_SUB;                  // "B operand"
+  static constexpr int STAGE_BYTES = B_BYTES + A_BYTES;
+  // as many stages as fit (6 for M <= 16): the bytes in flight per SM set the bandwidth
+  static constexpr int STAGES = (232448 - 2048) / STAGE_BYTES < 6 ? (232448 - 2048) / STAGE_BYTES : 6;
   static constexpr int OFF_STAGE = 0;
   // [cluster-1][128][MP] fp32 partials; reuses the stage ring once every rank's main loop
   // is over (the first cluster barrier of the epilogue).
   static constexpr int OFF_RED = 0;
   static constexpr int RED_SLOT_BYTES = SK_ROWS * MP * 4;
-  static constexpr int MAX_CLUSTER = (SK_STAGES * STAGE_BYTES) / RED_SLOT_BYTES + 1;
-  static constexpr int OFF_BAR = SK_STAGES * STAGE_BYTES;
-  static constexpr int OFF_MISC = OFF_BAR + (2 * SK_STAGES + 1) * 8;
+  static constexpr int MAX_CLUSTER = (STAGES * STAGE_BYTES) / RED_SLOT_BYTES + 1;
+  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+  static constexpr int OFF_MISC = OFF_BAR + (2 * STAGES + 1) * 8;
   static constexpr int TOTAL = OFF_MISC + 16;
   static constexpr int ALLOC = TOTAL + 1024;
   static constexpr uint32_t TMEM_COLS = MP <= 32 ? 32 : 64;
@@ -610,8 +615,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t* empty = full + SK_STAGES;
-  uint64_t* tfull = empty + SK_STAGES;
+  uint64_t* empty = full + L::STAGES;
+  uint64_t* tfull = empty + L::STAGES;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
@@ -620,12 +625,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int tile = blockIdx.x / csize;
-  const int num_kb = (K + BK - 1) / BK;
+  const int num_kb = (K + SK_BK - 1) / SK_BK;
   const int kb_begin = static_cast<int>((static_cast<int64_t>(rank) * num_kb) / csize);
   const int kb_end = static_cast<int>((static_cast<int64_t>(rank + 1) * num_kb) / csize);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < SK_STAGES; ++s) {
+    for (int s = 0; s < L::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -654,10 +659,17 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
       for (int kb = kb_begin; kb < kb_end; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, SITE_SKINNY_EMPTY)) break;
         uint8_t* st = smem + L::OFF_STAGE + stage * L::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[stage], L::B_BYTES + L::A_BYTES);
-        tma_load_2d(&tmB, &full[stage], st, kb * BK, tile * SK_ROWS);
-        tma_load_2d(&tmA, &full[stage], st + L::B_BYTES, kb * BK, 0);
-        if (++stage == SK_STAGES) {
+        // expect the full boxes: out-of-range parts are zero-filled and still counted
+        mbar_arrive_expect_tx(&full[stage], SK_SUB * (L::B_SUB + MP * BK * 2));
+#pragma unroll
+        for (int u = 0; u < SK_SUB; ++u) {
+          tma_load_2d(&tmB, &full[stage], st + u * L::B_SUB, kb * SK_BK + u * BK, tile * SK_ROWS);
+        }
+#pragma unroll
+        for (int u = 0; u < SK_SUB; ++u) {
+          tma_load_2d(&tmA, &full[stage], st + L::B_BYTES + u * L::A_SUB, kb * SK_BK + u * BK, 0);
+        }
+        if (++stage == L::STAGES) {
           stage = 0;
           phase ^= 1u;
         }
@@ -678,13 +690,15 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
         tc_fence_after();
         const uint32_t s0 = smem_u32(smem + L::OFF_STAGE + stage * L::STAGE_BYTES);
 #pragma unroll
-        for (int k = 0; k < BK / UMMA_K; ++k) {
-          const uint64_t ad = sdesc_sw128(s0 + k * UMMA_K * 2, 16, 1024);
-          const uint64_t bd = sdesc_sw128(s0 + L::B_BYTES + k * UMMA_K * 2, 16, 1024);
+        for (int k = 0; k < SK_BK / UMMA_K; ++k) {
+          const int u = k / (BK / UMMA_K), kk = k % (BK / UMMA_K);
+          const uint64_t ad = sdesc_sw128(s0 + u * L::B_SUB + kk * UMMA_K * 2, 16, 1024);
+          const uint64_t bd =
+              sdesc_sw128(s0 + L::B_BYTES + u * L::A_SUB + kk * UMMA_K * 2, 16, 1024);
           umma_f16(tmem_base, ad, bd, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
         }
         umma_commit(&empty[stage]);
-        if (++stage == SK_STAGES) {
+        if (++stage == L::STAGES) {
           stage = 0;
           phase ^= 1u;
         }
@@ -838,7 +852,7 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
   int s = set_smem(kernel, L::ALLOC);
   if (s != KTA_OK) return s;
   const int tiles = (N + SK_ROWS - 1) / SK_ROWS;
-  const int num_kb = (K + BK - 1) / BK;
+  const int num_kb = (K + SK_BK - 1) / SK_BK;
   const int sms = current_sm_count();
   // Cluster size: the largest power of two (<= 8) that keeps tiles x size within one wave
   // and leaves every rank at least two k-blocks.
@@ -942,6 +956,11 @@ inline int pair_mode() {
   return 1;
 }
 
+// gemm_m16.cu: M <= 16 on mma.sync over every SM (KTA_ERR_UNSUPPORTED when N is too large)
+template <bool BF16>
+int launch_m16(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda,
+               int64_t ldb, int64_t ldc, cudaStream_t stream);
+
 template <bool BF16, bool B_KMAJOR>
 int dispatch(const void* A, const void* B, void* C, int64_t M64, int64_t N64, int64_t K64,
              int64_t lda, int64_t ldb, int64_t ldc, void* stream_v) {
@@ -956,7 +975,11 @@ int dispatch(const void* A, const void* B, void* C, int64_t M64, int64_t N64, in
   const int M = static_cast<int>(M64), N = static_cast<int>(N64), K = static_cast<int>(K64);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (B_KMAJOR && M <= 64) {
-    if (M <= 16) return launch_skinny<16, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+    if (M <= 16) {
+      const int r = launch_m16<BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+      if (r != KTA_ERR_UNSUPPORTED) return r;
+      return launch_skinny<16, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+    }
     if (M <= 32) return launch_skinny<32, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
     if (M <= 48) return launch_skinny<48, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
     return launch_skinny<64, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);

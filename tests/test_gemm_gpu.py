@@ -80,6 +80,21 @@ def test_gemm_skinny(cuda_device, m, n, k):
     _check(c, ogemm.gemm_tn(a.double().numpy(), b.double().numpy()))
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m", [1, 5, 16])
+@pytest.mark.parametrize("n,k", [(1000, 200), (1184, 8200), (9472, 264), (16384, 512), (8, 16)])
+def test_gemm_m16_every_sm_path(cuda_device, m, n, k, dtype):
+    """M <= 16 runs on mma.sync with N cut into n8 tiles over one wave of CTAs: K tails
+    (200, 264, 8200 are not multiples of the 256-deep stage), N = 8 (one tile), N = 9472 (8
+    tiles on each of 148 SMs) and N = 16384 (more than one wave: the tensor-memory kernel)."""
+    from kta_b200 import ops
+
+    a, b = _inputs(m, n, k, dtype, seed=5)
+    c = ops.gemm(a.to(cuda_device), b.to(cuda_device))
+    torch.cuda.synchronize()
+    _check(c, ogemm.gemm_tn(a.double().numpy(), b.double().numpy()))
+
+
 def test_gemm_bf16_8192_sampled_rows(cuda_device):
     """The full 8192^3 bf16 config; 96 sampled rows checked against FP64."""
     from kta_b200 import ops
