@@ -13,9 +13,10 @@
 //     block = one 128-byte row per stage), warp 1 TMEM owner + single-thread
 //     `tcgen05.mma.kind::f8f6f4` issuer;
 //   * each K block's product goes to one of two TMEM partial buffers (2 x 256 columns), so
-//     the tensor core works on block kb+1 while eight promotion warps fold block kb into
-//     fp32 register accumulators: acc += partial * sa[m,kb] * sb[nb,kb] (each thread one row,
-//     128 columns of one weight block);
+//     the tensor core works on block kb+1 while sixteen promotion warps fold block kb into
+//     fp32 register accumulators: acc += partial * sa[m,kb] * sb[nb,kb] with packed f32x2
+//     FMAs (each thread one row, 64 columns inside one weight block; four warps per SMSP
+//     keep the TMEM loads of one warp behind the FMAs of the others);
 //   * the tile's accumulators go straight to global memory as bf16 rows;
 //   * every mbarrier wait is bounded.
 #include <algorithm>
@@ -32,7 +33,8 @@ constexpr int BN = 256;
 constexpr int BK = 128;               // e4m3 elements per stage = one scale block = 128 bytes
 constexpr int UMMA_K = 32;            // K per tcgen05.mma of kind::f8f6f4
 constexpr int STAGES = 4;
-constexpr int PROMO_WARPS = 8;
+constexpr int PROMO_WARPS = 16;      // four per SMSP: TMEM load latency hides behind FMAs
+constexpr int PROMO_COLS = 4 * BN / PROMO_WARPS;  // 64 columns of one row per thread
 constexpr int NUM_THREADS = 64 + PROMO_WARPS * 32;
 constexpr int GROUP_M = 16;
 
@@ -178,9 +180,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else {
-    // ---------------- promotion + epilogue: thread = output row, 128 columns ----------------
+    // ---------------- promotion + epilogue: thread = output row, 64 columns ----------------
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;  // which 128-column weight block of the tile
+    const int cg = (warp - 2) >> 2;    // 64-column group of the tile (0..3)
+    const int half = cg >> 1;          // which 128-column weight block of the tile
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     int buf = 0;
@@ -195,9 +198,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool blk_in = nblk < p.NB;
       const float* sa_row = p.sa + static_cast<long long>(row_in ? m : 0) * KB;
       const float* sb_row = p.sb + static_cast<long long>(blk_in ? nblk : 0) * KB;
-      float acc[128];
+      uint64_t acc[PROMO_COLS / 2];  // packed pairs of fp32 accumulators
 #pragma unroll
-      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+      for (int i = 0; i < PROMO_COLS / 2; ++i) acc[i] = 0ull;
       float scale_next = (row_in && blk_in) ? __ldg(sa_row) * __ldg(sb_row) : 0.f;
       for (int kb = 0; kb < KB; ++kb) {
         const float scale = scale_next;
@@ -209,15 +212,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t t = tmem + lane_base + buf * BN + half * 128;
+        const uint32_t t = tmem + lane_base + buf * BN + cg * PROMO_COLS;
+        const uint64_t s2 = f2(scale, scale);
 #pragma unroll
-        for (int c = 0; c < 128; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t + c, r);
+        for (int c = 0; c < PROMO_COLS; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t + c, r);
           tmem_ld_wait();
           reg_fence(r);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(__uint_as_float(r[i]), scale, acc[c + i]);
+          for (int i = 0; i < 8; ++i) {
+            acc[c / 2 + i] = fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), s2,
+                                  acc[c / 2 + i]);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -226,17 +233,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (buf == 0) bphase ^= 1u;
       }
       if (!ok) break;
-      const int n0 = nb * BN + half * 128;
+      const int n0 = nb * BN + cg * PROMO_COLS;
       if (row_in && n0 < p.N) {
         __nv_bfloat16* crow = p.c + static_cast<long long>(m) * p.N + n0;
+        uint32_t pk[PROMO_COLS / 2];
 #pragma unroll
-        for (int c = 0; c < 128; c += 8) {
+        for (int i = 0; i < PROMO_COLS / 2; ++i) {
+          float x0, x1;
+          f2_split(acc[i], x0, x1);
+          pk[i] = pack_bf16x2(x0, x1);
+        }
+#pragma unroll
+        for (int c = 0; c < PROMO_COLS; c += 8) {
           if (n0 + c < p.N) {
-            const uint4 v = make_uint4(pack_bf16x2(acc[c], acc[c + 1]),
-                                       pack_bf16x2(acc[c + 2], acc[c + 3]),
-                                       pack_bf16x2(acc[c + 4], acc[c + 5]),
-                                       pack_bf16x2(acc[c + 6], acc[c + 7]));
-            *reinterpret_cast<uint4*>(crow + c) = v;
+            *reinterpret_cast<uint4*>(crow + c) =
+                make_uint4(pk[c / 2], pk[c / 2 + 1], pk[c / 2 + 2], pk[c / 2 + 3]);
           }
         }
       }
