@@ -55,7 +55,7 @@ constexpr int V_PRODUCER_WARP = 10;
 constexpr int SOFTMAX_REGS = 208;       // 2 x 128 x 208 + 128 x 88 = 384 x 168 (launch)
 constexpr int OTHER_REGS = 88;
 // exponentials evaluated on the FMA pipe, per 8 column pairs of an off-diagonal tile
-constexpr int EXP_POLY_PER_8 = 3;
+constexpr int EXP_POLY_PER_8 = 2;
 constexpr int HALF = 128 * 64 * 2;      // [128 rows][64 d] bf16, one swizzle column
 constexpr int TILE = 2 * HALF;          // [128 rows][128 d]
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: rescale when the max grew > 2^8
