@@ -13,6 +13,9 @@ import torch
 from kta_b200 import lib
 
 
+# size of the library-owned partials array behind kta_decode_gqa_bf16_noalloc
+NOALLOC_BYTES = 8 << 20
+
 def _stream() -> int:
     return int(torch.cuda.current_stream().cuda_stream)
 
@@ -129,7 +132,10 @@ def decode_gqa(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                workspace: torch.Tensor | None = None) -> torch.Tensor:
     """GQA decode: Q bf16 [B, Hq, D]; caches bf16 [T, Hkv, D] with sequence b at rows
     kv_offsets[b] .. kv_offsets[b] + seqlens[b]; seqlens int32 [B], kv_offsets int64 [B].
-    ``workspace`` (uint8, zero-initialised once) may be reused across calls on one stream."""
+    ``workspace`` (uint8, zero-initialised once) may be reused across calls on one stream.
+    Without one, the library's own 8 MiB array is used when the split partials fit
+    (kta_decode_gqa_bf16_noalloc: no allocation, no extra kernel; calls that overlap on the
+    GPU then share it, so concurrent streams should pass their own workspace)."""
     _need_cuda(q, k_cache, v_cache, seqlens, kv_offsets)
     if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or \
             v_cache.dtype != torch.bfloat16:
@@ -148,6 +154,11 @@ def decode_gqa(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     if out is None:
         out = torch.empty_like(q)
     need = decode_workspace_bytes(bsz, hq, hkv, d, max_seqlen)
+    if workspace is None and need <= NOALLOC_BYTES:
+        lib.call("kta_decode_gqa_bf16_noalloc", q.data_ptr(), k_cache.data_ptr(),
+                 v_cache.data_ptr(), seqlens.data_ptr(), kv_offsets.data_ptr(), out.data_ptr(),
+                 bsz, hq, hkv, d, k_cache.shape[0], int(max_seqlen), float(scale), _stream())
+        return out
     if workspace is None:
         workspace = torch.zeros(max(need, 1), dtype=torch.uint8, device=q.device)
     if workspace.numel() < need:

@@ -37,9 +37,11 @@ def _attn(t, shape, out):
 
 
 def _decode(t, shape, out):
+    # max_seqlen comes from the host (run() fills it in): a device reduction here would be a
+    # kernel outside the library inside the entry's launch
     return {"O": ops.decode_gqa(t["Q"], t["Kc"], t["Vc"], t["seqlens"], t["kv_offsets"],
-                                int(shape.get("max_seqlen", int(t["seqlens"].max()))),
-                                scale=shape["D"] ** -0.5, out=out["O"])}
+                                int(shape["max_seqlen"]), scale=shape["D"] ** -0.5,
+                                out=out["O"])}
 
 
 RUNNERS: dict[str, Callable[..., dict[str, torch.Tensor]]] = {
@@ -57,13 +59,18 @@ _TORCH = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32,
 
 
 def run(entry: str, problem: Problem, shape: dict[str, Any], data: dict[str, np.ndarray],
-        nan_fill: bool = True, raw: bool = False, device: str = "cuda"
-        ) -> dict[str, Any]:
-    """Outputs of one launch as float64 numpy arrays (``raw``: device tensors)."""
+        nan_fill: bool = True, raw: bool = False, device: str = "cuda",
+        launched: list[str] | None = None) -> dict[str, Any]:
+    """Outputs of one launch as float64 numpy arrays (``raw``: device tensors). With
+    ``launched``, the names of the GPU kernels the entry itself launched are appended to it
+    (a CUPTI trace through torch.profiler around the launch only; memsets and copies are not
+    kernels)."""
     from kta_b200 import inputs as kinp
 
     if entry not in RUNNERS:
         raise ValueError(f"no runner for entry {entry!r}")
+    if "seqlens" in data and "max_seqlen" not in shape:
+        shape = {**shape, "max_seqlen": int(np.max(data["seqlens"], initial=0))}
     dtypes = {t.name: t.dtype for t in problem.inputs}
     tens = {name: to_torch(arr, dtypes[name], device) for name, arr in data.items()}
     outs: dict[str, torch.Tensor] = {}
@@ -73,8 +80,19 @@ def run(entry: str, problem: Problem, shape: dict[str, Any], data: dict[str, np.
         if nan_fill:
             buf.view(torch.uint8).fill_(NAN_BYTE)
         outs[t.name] = buf
-    got = RUNNERS[entry](tens, shape, outs)
-    torch.cuda.synchronize()
+    if launched is None:
+        got = RUNNERS[entry](tens, shape, outs)
+        torch.cuda.synchronize()
+    else:
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            got = RUNNERS[entry](tens, shape, outs)
+            torch.cuda.synchronize()
+        for ev in prof.events():
+            if ev.device_type.name == "CUDA" and not ev.name.startswith(("Memset", "Memcpy")):
+                launched.append(ev.name)
     if raw:
         return got
     return {name: v.to(torch.float64).cpu().numpy() for name, v in got.items()}

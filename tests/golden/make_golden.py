@@ -18,7 +18,9 @@ What it records, each from the reference itself:
   cases' `C = A @ B` and the B200 `C = A @ B.T`), the causal attention, decode and FP8
   statements of kta_b200/cases (small shapes);
 - schemas.json: whether each kta_b200 case file's problem / contract / case validate in
-  the reference's pydantic records.
+  the reference's pydantic records;
+- hidden.json: `kta.checks.hidden.hidden_shapes` for fixed seeds and base shapes, and
+  `kta.checks.full.in_scope` on static, range and unscoped contracts.
 """
 
 from __future__ import annotations
@@ -147,6 +149,29 @@ def main(ref_root: str) -> int:
             res["case_record"] = f"error: {type(exc).__name__}"
         schemas.append(res)
     (HERE / "schemas.json").write_text(json.dumps(schemas, indent=1))
+
+    # ---- hidden shapes and shape scope (the full check's shape selection) ----
+    from kta.checks import hidden as chidden
+    from kta.checks.full import in_scope as ref_in_scope
+
+    hidden_cases = []
+    for seed in ("0123456789abcdef0123456789abcdef", "feedface" * 4):
+        for base in ({"M": 8192, "N": 8192, "K": 8192}, {"M": 16, "N": 8192, "K": 8192},
+                     {"B": 8, "H": 32, "S": 4096, "D": 128}, {"M": 1024, "N": 1024, "K": 1024,
+                                                            "dtype": "f16"}):
+            got = chidden.hidden_shapes(seed, base)
+            hidden_cases.append({"seed": seed, "base": base,
+                                 "shapes": [[s, c] for s, c in got]})
+    scopes = []
+    own = [{"M": 64, "N": 64, "K": 64}, {"M": 128, "N": 256, "K": 64}]
+    for scope in ({}, {"kind": "static"}, {"kind": "range", "ranges": {"M": [1, 100]}},
+                  {"kind": "range", "ranges": {"M": [1, 4096], "K": [64, 64]}}):
+        for shape in ({"M": 64, "N": 64, "K": 64}, {"M": 65, "N": 64, "K": 64},
+                      {"M": 128, "N": 256, "K": 64}, {"M": 3, "N": 5, "K": 7}):
+            scopes.append({"scope": scope, "own": own, "shape": shape,
+                           "in_scope": ref_in_scope(shape, scope, own)})
+    (HERE / "hidden.json").write_text(json.dumps({"hidden": hidden_cases, "scope": scopes},
+                                                 indent=1))
 
     # ---- the reference's statement runner on the CPU ----
     script_src = (ref / "src" / "kta" / "checks" / "scripts" / "ref_torch.py").read_text()

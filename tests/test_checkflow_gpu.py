@@ -1,0 +1,36 @@
+"""The quick gate and the full check through libkta_b200 on the GPU: numeric on the
+contract's distributions against the FP64 reference, the anti-cheat checks (only this
+library's kernels launched, byte-identical repeat, no forbidden libraries linked)."""
+
+from __future__ import annotations
+
+import pytest
+
+from kta_b200 import checkflow, schemas
+
+pytestmark = pytest.mark.gpu
+
+
+def test_quick_check_gemm_f16(cuda_device):
+    cf = schemas.load_case_file("gemm_f16_1024")
+    res = checkflow.quick_check(cf)
+    assert res["passed"], res["failures"]
+    assert res["sub_checks"] == {"numeric": True, "anticheat": True}
+
+
+def test_full_check_attention_small_shape(cuda_device):
+    cf = schemas.load_case_file("attn_causal")
+    res = checkflow.full_check(cf, {"B": 1, "H": 2, "S": 384, "D": 128},
+                               hidden_seed="0" * 32)
+    assert res["passed"], res["failures"]
+    assert res["detail"]["dists"] == cf.contract.input_dists
+    # static scope: the hidden shapes are listed, not run
+    assert res["detail"]["out_of_scope"] == list(checkflow.HIDDEN_CATEGORIES)
+
+
+def test_anticheat_sees_only_library_kernels(cuda_device):
+    cf = schemas.load_case_file("decode_gqa")
+    shape = checkflow.case_shapes(cf)[0]
+    small = {**shape, "B": 3, "max_seqlen": 300}
+    res = checkflow.quick_check(cf, small)
+    assert res["passed"], res["failures"]
