@@ -20,7 +20,10 @@ What it records, each from the reference itself:
 - schemas.json: whether each kta_b200 case file's problem / contract / case validate in
   the reference's pydantic records;
 - hidden.json: `kta.checks.hidden.hidden_shapes` for fixed seeds and base shapes, and
-  `kta.checks.full.in_scope` on static, range and unscoped contracts.
+  `kta.checks.full.in_scope` on static, range and unscoped contracts;
+- hwarch.json: kta_b200/hardware/arch_sm100.yaml and model_b200_sm100.yaml validated as the
+  reference's HwArch and HwModel and resolved by its `MachineModel.build`: each resource's
+  rate and status, the walls' limits and the operation classes.
 """
 
 from __future__ import annotations
@@ -172,6 +175,24 @@ def main(ref_root: str) -> int:
                            "in_scope": ref_in_scope(shape, scope, own)})
     (HERE / "hidden.json").write_text(json.dumps({"hidden": hidden_cases, "scope": scopes},
                                                  indent=1))
+
+    # ---- the sm100 architecture class and the B200 instance in the reference's schema ----
+    from kta.core.schemas.hwmodel import HwArch
+    from kta.models.machine import MachineModel
+
+    hw_dir = REPO / "kta_b200" / "hardware"
+    arch = HwArch.model_validate(yaml.safe_load((hw_dir / "arch_sm100.yaml").read_text()))
+    inst = HwModel.model_validate(yaml.safe_load((hw_dir / "model_b200_sm100.yaml").read_text()))
+    mm = MachineModel.build(inst, arch)
+    hwrec = {
+        "arch": arch.ref,
+        "resources": {k: {"rate": r.rate, "status": r.status, "scope": r.scope,
+                          "amount": r.amount} for k, r in sorted(mm.resources.items())},
+        "walls": {w.spec.name: w.limit for w in mm.walls},
+        "op_classes": sorted(mm.op_classes),
+        "scope_counts": dict(mm.scope_counts),
+    }
+    (HERE / "hwarch.json").write_text(json.dumps(hwrec, indent=1))
 
     # ---- the reference's statement runner on the CPU ----
     script_src = (ref / "src" / "kta" / "checks" / "scripts" / "ref_torch.py").read_text()
