@@ -83,6 +83,12 @@ class Measurement(Body):
     protocol: str
 
 
+class Profile(Body):
+    """Nsight Compute metrics of one launch (src/kta/core/schemas/evaluation.py:100-101)."""
+
+    metrics: dict[str, float] = Field(default_factory=dict)
+
+
 class Bound(Body):
     per_unit_us: dict[Unit, float] = Field(default_factory=dict)
     bound_us: float

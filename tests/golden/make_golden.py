@@ -23,7 +23,9 @@ What it records, each from the reference itself:
   `kta.checks.full.in_scope` on static, range and unscoped contracts;
 - hwarch.json: kta_b200/hardware/arch_sm100.yaml and model_b200_sm100.yaml validated as the
   reference's HwArch and HwModel and resolved by its `MachineModel.build`: each resource's
-  rate and status, the walls' limits and the operation classes.
+  rate and status, the walls' limits and the operation classes;
+- ncu.json: `kta.measure.profile.parse_ncu_csv` on ncu_launches_decode.csv (a launch list
+  this build captured on a B200 with `ncu --csv`) for several kernel names.
 """
 
 from __future__ import annotations
@@ -193,6 +195,14 @@ def main(ref_root: str) -> int:
         "scope_counts": dict(mm.scope_counts),
     }
     (HERE / "hwarch.json").write_text(json.dumps(hwrec, indent=1))
+
+    # ---- ncu CSV ingestion ----
+    from kta.measure.profile import parse_ncu_csv
+
+    text = (HERE / "ncu_launches_decode.csv").read_text()
+    parsed = {k: parse_ncu_csv(text, k) for k in ("decode_kernel", "kta::", "FillFunctor",
+                                                  "no_such_kernel", "")}
+    (HERE / "ncu.json").write_text(json.dumps(parsed, indent=1, sort_keys=True))
 
     # ---- the reference's statement runner on the CPU ----
     script_src = (ref / "src" / "kta" / "checks" / "scripts" / "ref_torch.py").read_text()
