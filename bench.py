@@ -664,6 +664,100 @@ class Fp8Workload:
                             f"rows (of {self.m}), N={self.n_total}, K={self.k}")
 
 
+class RowOpWorkload:
+    """Row RMSNorm or softmax over X [M, N] f16 (KTA's test-set rmsnorm / softmax,
+    perfmodel/testset/gen.py:662-704, :781-807) at an HBM-bound size; this rank's row shard.
+    HBM-bound: X read once, Y written once (W once for RMSNorm)."""
+
+    unit = "GB/s"
+    dtype_name = "f16"
+    graph_default = False
+    hbm_bound = True
+
+    def __init__(self, op: str, dist: Dist, m: int = 65536, n: int = 4096) -> None:
+        self.op, self.m_total, self.n = op, m, n
+        lo, hi = shard(m, dist.world, dist.rank)
+        self.m = hi - lo
+        self.case = f"{op}_f16"
+        self.kernel_regex = "rowop_kernel"
+
+    @property
+    def flops(self) -> float:
+        return 0.0
+
+    @property
+    def bytes(self) -> float:
+        return float(2 * self.m * self.n * 2 + (self.n * 2 if self.op == "rmsnorm" else 0))
+
+    def work(self) -> float:
+        return self.bytes
+
+    def sol_shape(self) -> dict:
+        return {"M": self.m, "N": self.n}
+
+    def config(self, world: int) -> dict:
+        what = ("Y = X * rsqrt(mean(X^2) + 1e-6) * W" if self.op == "rmsnorm"
+                else "Y = softmax(X) per row")
+        return {"workload": f"{self.op}_f16: {what}, f16, M={self.m_total} N={self.n}, fp32 "
+                            "statistics",
+                "case": self.case, "M": self.m_total, "N": self.n,
+                "global_batch": self.m_total, "seq_len": None,
+                "parallelism": f"row shards x{world} (no collective)",
+                "l2": "inputs larger than L2: 4 rotating X/Y sets (512 MB each), no flush",
+                "inputs": "N(0,1) f16 from a seeded torch generator"}
+
+    def setup(self, device: torch.device) -> None:
+        g = torch.Generator(device=device).manual_seed(4321)
+        self.x = [_randn((self.m, self.n), torch.float16, g) for _ in range(NSETS)]
+        self.y = [torch.empty((self.m, self.n), dtype=torch.float16, device=device)
+                  for _ in range(NSETS)]
+        self.w = _randn((self.n,), torch.float16, g)
+
+    def _run(self, x, y) -> None:
+        from kta_b200 import ops
+
+        if self.op == "rmsnorm":
+            ops.rmsnorm(x, self.w, 1e-6, out=y)
+        else:
+            ops.softmax(x, out=y)
+
+    def launch(self, i: int) -> None:
+        j = i % NSETS
+        self._run(self.x[j], self.y[j])
+
+    def setup_e2e(self, device: torch.device) -> None:
+        g = torch.Generator().manual_seed(99)
+        self.hx = _randn((self.m, self.n), torch.float16, g, device="cpu").pin_memory()
+        self.hy = torch.empty((self.m, self.n), dtype=torch.float16).pin_memory()
+        self.dx = torch.empty_like(self.hx, device=device)
+        self.dy = torch.empty_like(self.hy, device=device)
+        self.h2d_bytes = self.hx.numel() * 2
+        self.d2h_bytes = self.hy.numel() * 2
+
+    def e2e_step(self) -> None:
+        self.dx.copy_(self.hx, non_blocking=True)
+        self._run(self.dx, self.dy)
+        self.hy.copy_(self.dy, non_blocking=True)
+
+    def cpu_sample(self, rows: int):
+        rows = max(1, min(rows, self.m_total))
+        g = torch.Generator().manual_seed(7)
+        x = _randn((rows, self.n), torch.float16, g, device="cpu")
+        w = _randn((self.n,), torch.float16, g, device="cpu")
+
+        def run():
+            from kta_b200 import schemas
+            from oracle import statement
+
+            stmt = schemas.load_case_file(self.case).problem.reference_impl
+            tensors = {"X": x, "W": w} if self.op == "rmsnorm" else {"X": x}
+            statement.run_library(stmt, tensors, {"M": rows, "N": self.n})
+
+        units = float(2 * rows * self.n * 2)
+        return run, units, (f"{self.op} statement in f16 on the host for {rows} of "
+                            f"{self.m_total} rows, N={self.n}")
+
+
 WORKLOADS = {
     "gemm_bf16_8192": lambda d: GemmWorkload("gemm_bf16_8192", 8192, 8192, 8192,
                                              torch.bfloat16, d, "gemm_bf16_8192"),
@@ -674,6 +768,8 @@ WORKLOADS = {
     "decode_gqa": lambda d: DecodeWorkload(d),
     "attn_causal": lambda d: AttnWorkload(d),
     "gemm_fp8": lambda d: Fp8Workload(d),
+    "rmsnorm_f16": lambda d: RowOpWorkload("rmsnorm", d),
+    "softmax_f16": lambda d: RowOpWorkload("softmax", d),
 }
 
 

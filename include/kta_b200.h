@@ -132,6 +132,21 @@ int kta_decode_gqa_bf16_noalloc(const void* Q, const void* Kc, const void* Vc,
                                 int64_t Hq, int64_t Hkv, int64_t D, int64_t cache_tokens,
                                 int64_t max_seqlen, float scale, void* stream);
 
+/* Row RMSNorm: Y[m, :] = X[m, :] * rsqrt(mean_j X[m, j]^2 + eps) * W, fp32 statistics,
+ * X, Y [M, N] and W [N] row-major f16 or bf16. Replaces KTA's test-set rmsnorm
+ * (perfmodel/testset/gen.py:662-704, eps 1e-6 there). N % 8 == 0, N <= 16384, 16-byte
+ * aligned X, W, Y; eps >= 0. */
+int kta_rmsnorm_f16(const void* X, const void* W, void* Y, int64_t M, int64_t N, float eps,
+                    void* stream);
+int kta_rmsnorm_bf16(const void* X, const void* W, void* Y, int64_t M, int64_t N, float eps,
+                     void* stream);
+
+/* Row softmax: Y[m, :] = softmax(X[m, :]) via 2^(x log2 e - max), fp32 max and sum, X, Y
+ * [M, N] row-major f16 or bf16. Replaces KTA's test-set softmax
+ * (perfmodel/testset/gen.py:781-807). N % 8 == 0, N <= 16384, 16-byte aligned X, Y. */
+int kta_softmax_f16(const void* X, void* Y, int64_t M, int64_t N, void* stream);
+int kta_softmax_bf16(const void* X, void* Y, int64_t M, int64_t N, void* stream);
+
 /* --- Reference-compatible `so` shims -----------------------------------------------------
  * The exact signature src/kta/measure/bench.py:80-98 calls: pointers as uint64 device
  * addresses, shape scalars as int32, restype None, default stream, the caller synchronises.
@@ -141,6 +156,10 @@ void kta_so_gemm_bf16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, 
 void kta_so_gemm_f16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K);
 void kta_so_gemm_nn_f16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K);
 void kta_so_gemm_nn_bf16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t N, int32_t K);
+/* the test set's rmsnorm (eps 1e-6) and softmax, f16, with its (X, W, Y, M, N) / (X, Y, M, N)
+ * parameters (perfmodel/testset/gen.py:662-704, :781-807) */
+void kta_so_rmsnorm_f16(uint64_t X, uint64_t W, uint64_t Y, int32_t M, int32_t N);
+void kta_so_softmax_f16(uint64_t X, uint64_t Y, int32_t M, int32_t N);
 
 /* Status of the last kta_so_* call on this host thread. */
 int kta_last_error(void);

@@ -95,6 +95,40 @@ def gemm_fp8_blockscaled(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb:
     return out
 
 
+def _rowop_check(x: torch.Tensor, name: str) -> None:
+    if x.dim() != 2 or not x.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous [M, N] tensor")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"{name} must be f16 or bf16")
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Y = X * rsqrt(mean(X^2, -1) + eps) * W over the rows of X [M, N] (f16 or bf16), W [N]
+    of the same dtype; fp32 statistics."""
+    _need_cuda(x, w)
+    _rowop_check(x, "X")
+    if w.dtype != x.dtype or w.shape != (x.shape[1],) or not w.is_contiguous():
+        raise ValueError("W must be a contiguous [N] tensor of X's dtype")
+    if out is None:
+        out = torch.empty_like(x)
+    entry = "kta_rmsnorm_f16" if x.dtype == torch.float16 else "kta_rmsnorm_bf16"
+    lib.call(entry, x.data_ptr(), w.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1],
+             float(eps), _stream())
+    return out
+
+
+def softmax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Row softmax of X [M, N] (f16 or bf16), fp32 max and sum."""
+    _need_cuda(x)
+    _rowop_check(x, "X")
+    if out is None:
+        out = torch.empty_like(x)
+    entry = "kta_softmax_f16" if x.dtype == torch.float16 else "kta_softmax_bf16"
+    lib.call(entry, x.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1], _stream())
+    return out
+
+
 def attn_fwd_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None,
                     out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
                     ) -> tuple[torch.Tensor, torch.Tensor]:

@@ -44,7 +44,19 @@ def _decode(t, shape, out):
                                 out=out["O"])}
 
 
+def _rms(t, shape, out):
+    return {"Y": ops.rmsnorm(t["X"], t["W"], eps=1e-6, out=out["Y"])}
+
+
+def _softmax(t, shape, out):
+    return {"Y": ops.softmax(t["X"], out=out["Y"])}
+
+
 RUNNERS: dict[str, Callable[..., dict[str, torch.Tensor]]] = {
+    "kta_rmsnorm_f16": _rms,
+    "kta_rmsnorm_bf16": _rms,
+    "kta_softmax_f16": _softmax,
+    "kta_softmax_bf16": _softmax,
     "kta_gemm_bf16": _gemm("kta_gemm_bf16"),
     "kta_gemm_f16": _gemm("kta_gemm_f16"),
     "kta_gemm_nn_bf16": _gemm("kta_gemm_nn_bf16"),

@@ -282,6 +282,16 @@ def main(ref_root: str) -> int:
     st_out.update({"fp8.A": af, "fp8.B": bf, "fp8.sa": sa, "fp8.sb": sb})
     st_out.update(run("fp8", case_statement("gemm_fp8_blockscaled"), dims,
                       {"A": af, "sa": sa, "B": bf, "sb": sb}, ["C"], library=False))
+    dims = {"M": 12, "N": 40}
+    xr = gen("X", ["M", "N"], "f16")
+    wr = gen("W", ["N"], "f16")
+    st_out.update({"rms.X": xr, "rms.W": wr})
+    st_out.update(run("rms", case_statement("rmsnorm_f16"), dims, {"X": xr, "W": wr}, ["Y"],
+                      library=False))
+    xs = gen("X", ["M", "N"], "f16", dist="large_dynamic_range")
+    st_out.update({"smax.X": xs})
+    st_out.update(run("smax", case_statement("softmax_f16"), dims, {"X": xs}, ["Y"],
+                      library=False))
     np.savez(HERE / "statements.npz", **st_out)
     shutil.rmtree(work_dir)
     print("wrote", sorted(p.name for p in HERE.iterdir()))

@@ -105,6 +105,23 @@ def test_fp8_argument_checks():
     assert L.kta_gemm_fp8_blockscaled(*a, 0, 128, 128, None) == 1
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_rowop_argument_checks(dt):
+    L = lib.load()
+    rms = getattr(L, f"kta_rmsnorm_{dt}")
+    smx = getattr(L, f"kta_softmax_{dt}")
+    a = ALIGNED
+    assert rms(a, a, a, 64, 100, 1e-6, None) == 3        # N % 8
+    assert rms(a, a, a, 64, 16392, 1e-6, None) == 2      # N > 16384
+    assert rms(a, None, a, 64, 64, 1e-6, None) == 1      # W missing
+    assert rms(a, a, a, 0, 64, 1e-6, None) == 1          # M = 0
+    assert rms(a, a, a, 64, 64, -1.0, None) == 1         # eps < 0
+    assert rms(MISALIGNED, a, a, 64, 64, 1e-6, None) == 3
+    assert smx(a, a, 64, 100, None) == 3
+    assert smx(None, a, 64, 64, None) == 1
+    assert smx(a, MISALIGNED, 64, 64, None) == 3
+
+
 def test_so_shim_reports_through_last_error():
     L = lib.load()
     L.kta_so_gemm_f16(0, 0, 0, 64, 64, 64)

@@ -112,3 +112,19 @@ def test_bf16_widening_and_rounding_match_torch():
     assert np.array_equal(bits.view(np.int16), t)
     back = numerics.bf16_bits_to_f64(bits)
     assert np.array_equal(back, torch.from_numpy(t).view(torch.bfloat16).double().numpy())
+
+
+def test_rmsnorm_matches_reference_statement_runner(st):
+    from oracle import rowops
+
+    x, w = st["rms.X"], st["rms.W"]
+    np.testing.assert_allclose(rowops.rmsnorm(x, w, 1e-6), st["rms.Y.f64"].reshape(x.shape),
+                               rtol=1e-12, atol=1e-12)
+
+
+def test_softmax_matches_reference_statement_runner(st):
+    from oracle import rowops
+
+    x = st["smax.X"]
+    np.testing.assert_allclose(rowops.softmax(x), st["smax.Y.f64"].reshape(x.shape),
+                               rtol=1e-12, atol=1e-15)
