@@ -664,6 +664,99 @@ class Fp8Workload:
                             f"rows (of {self.m}), N={self.n_total}, K={self.k}")
 
 
+class MoeWorkload:
+    """MoE expert GEMM (KTA's moe_gemm, perfmodel/testset/gen.py:332-356) at the test set's
+    shape E=8 T=2048 N=1024 K=2048, f16: T / E tokens per expert, W [E, K, N]; this rank's
+    expert shard (experts are independent)."""
+
+    kernel_regex = "gemm_kernel"
+    unit = "TFLOP/s"
+    dtype_name = "f16"
+    case = "moe_gemm_f16"
+    graph_default = True  # a few microseconds per launch: shorter than the host launch path
+
+    def __init__(self, dist: Dist, e: int = 8, t: int = 2048, n: int = 1024, k: int = 2048):
+        self.e_total, self.t_total, self.n, self.k = e, t, n, k
+        lo, hi = shard(e, dist.world, dist.rank)
+        self.e = max(hi - lo, 0)
+        self.t = self.e * (t // e)
+        self.m = self.t
+
+    @property
+    def flops(self) -> float:
+        return 2.0 * self.t * self.n * self.k
+
+    @property
+    def bytes(self) -> float:
+        return float((self.t * self.k + self.e * self.k * self.n + self.t * self.n) * 2)
+
+    def work(self) -> float:
+        return self.flops
+
+    def sol_shape(self) -> dict:
+        return {"E": self.e, "T": self.t, "N": self.n, "K": self.k}
+
+    def config(self, world: int) -> dict:
+        return {"workload": f"moe_gemm_f16: E={self.e_total} T={self.t_total} N={self.n} "
+                            f"K={self.k}, f16, fp32 accumulate",
+                "case": self.case, "E": self.e_total, "T": self.t_total, "N": self.n,
+                "K": self.k, "global_batch": self.t_total, "seq_len": None,
+                "parallelism": f"expert shards x{world} (no collective)",
+                "l2": "4 rotating input sets of 25 MB (L2-resident: the test set's warm case)",
+                "inputs": "N(0,1)/sqrt(K) f16 from a seeded torch generator"}
+
+    def setup(self, device: torch.device) -> None:
+        g = torch.Generator(device=device).manual_seed(2468)
+        s = 1.0 / math.sqrt(self.k)
+        self.a = [_randn((self.t, self.k), torch.float16, g, s) for _ in range(NSETS)]
+        self.w = [_randn((self.e, self.k, self.n), torch.float16, g, s) for _ in range(NSETS)]
+        self.c = [torch.empty((self.t, self.n), dtype=torch.float16, device=device)
+                  for _ in range(NSETS)]
+
+    def launch(self, i: int) -> None:
+        from kta_b200 import ops
+
+        j = i % NSETS
+        ops.moe_gemm(self.a[j], self.w[j], out=self.c[j])
+
+    def setup_e2e(self, device: torch.device) -> None:
+        g = torch.Generator().manual_seed(99)
+        s = 1.0 / math.sqrt(self.k)
+        self.ha = _randn((self.t, self.k), torch.float16, g, s, device="cpu").pin_memory()
+        self.hw = _randn((self.e, self.k, self.n), torch.float16, g, s, device="cpu").pin_memory()
+        self.hc = torch.empty((self.t, self.n), dtype=torch.float16).pin_memory()
+        self.da = torch.empty_like(self.ha, device=device)
+        self.dw = torch.empty_like(self.hw, device=device)
+        self.dc = torch.empty_like(self.hc, device=device)
+        self.h2d_bytes = (self.ha.numel() + self.hw.numel()) * 2
+        self.d2h_bytes = self.hc.numel() * 2
+
+    def e2e_step(self) -> None:
+        from kta_b200 import ops
+
+        self.da.copy_(self.ha, non_blocking=True)
+        self.dw.copy_(self.hw, non_blocking=True)
+        ops.moe_gemm(self.da, self.dw, out=self.dc)
+        self.hc.copy_(self.dc, non_blocking=True)
+
+    def cpu_sample(self, rows: int):
+        g = torch.Generator().manual_seed(7)
+        s = 1.0 / math.sqrt(self.k)
+        per = self.t_total // self.e_total
+        rows = max(1, min(rows, per))
+        a = _randn((rows, self.k), torch.float16, g, s, device="cpu")
+        w = _randn((self.k, self.n), torch.float16, g, s, device="cpu")
+
+        def run():
+            from oracle import statement
+
+            statement.run_library("C = A @ W", {"A": a, "W": w}, {})
+
+        units = 2.0 * rows * self.n * self.k
+        return run, units, (f"one expert's A @ W[e] in f16 on the host, {rows} of its {per} "
+                            f"rows, N={self.n}, K={self.k}")
+
+
 class RowOpWorkload:
     """Row RMSNorm or softmax over X [M, N] f16 (KTA's test-set rmsnorm / softmax,
     perfmodel/testset/gen.py:662-704, :781-807) at an HBM-bound size; this rank's row shard.
@@ -768,6 +861,7 @@ WORKLOADS = {
     "decode_gqa": lambda d: DecodeWorkload(d),
     "attn_causal": lambda d: AttnWorkload(d),
     "gemm_fp8": lambda d: Fp8Workload(d),
+    "moe_gemm_f16": lambda d: MoeWorkload(d),
     "rmsnorm_f16": lambda d: RowOpWorkload("rmsnorm", d),
     "softmax_f16": lambda d: RowOpWorkload("softmax", d),
 }

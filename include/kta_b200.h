@@ -132,6 +132,16 @@ int kta_decode_gqa_bf16_noalloc(const void* Q, const void* Kc, const void* Vc,
                                 int64_t Hq, int64_t Hkv, int64_t D, int64_t cache_tokens,
                                 int64_t max_seqlen, float scale, void* stream);
 
+/* MoE expert GEMM: tokens grouped by expert, T / E rows each; for every expert e,
+ * C[e*T/E : (e+1)*T/E, :] = A[e*T/E : (e+1)*T/E, :] . W[e] with A [T, K], W [E, K, N] and C
+ * [T, N] row-major f16 or bf16, fp32 accumulate. Replaces KTA's test-set moe_gemm
+ * (perfmodel/testset/gen.py:332-356). T % E == 0 and (T / E) % 128 == 0; K % 8 == 0 and
+ * N % 8 == 0; 16-byte aligned A, W, C. One launch over every expert. */
+int kta_moe_gemm_f16(const void* A, const void* W, void* C, int64_t E, int64_t T, int64_t N,
+                     int64_t K, void* stream);
+int kta_moe_gemm_bf16(const void* A, const void* W, void* C, int64_t E, int64_t T, int64_t N,
+                      int64_t K, void* stream);
+
 /* Row RMSNorm: Y[m, :] = X[m, :] * rsqrt(mean_j X[m, j]^2 + eps) * W, fp32 statistics,
  * X, Y [M, N] and W [N] row-major f16 or bf16. Replaces KTA's test-set rmsnorm
  * (perfmodel/testset/gen.py:662-704, eps 1e-6 there). N % 8 == 0, N <= 16384, 16-byte
@@ -159,6 +169,9 @@ void kta_so_gemm_nn_bf16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t 
 /* the test set's rmsnorm (eps 1e-6) and softmax, f16, with its (X, W, Y, M, N) / (X, Y, M, N)
  * parameters (perfmodel/testset/gen.py:662-704, :781-807) */
 void kta_so_rmsnorm_f16(uint64_t X, uint64_t W, uint64_t Y, int32_t M, int32_t N);
+/* the test set's moe_gemm, f16, with its (A, W, C) tensors and (E, T, N, K) sizes */
+void kta_so_moe_gemm_f16(uint64_t A, uint64_t W, uint64_t C, int32_t E, int32_t T, int32_t N,
+                         int32_t K);
 void kta_so_softmax_f16(uint64_t X, uint64_t Y, int32_t M, int32_t N);
 
 /* Status of the last kta_so_* call on this host thread. */

@@ -84,7 +84,7 @@ template <int BN, int STAGES, bool BF16, bool B_KMAJOR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
-                unsigned int* status) {
+                int rows_per_group, unsigned int* status) {
   using L = Layout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -151,9 +151,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tma_load_2d(&tmB, &full[stage], sb, kb * BK, nb * BN);
           } else {
             // [K,N] row-major: BN/64 boxes of 64 N x 64 K, each one MN-major swizzle block.
+            // Grouped (MoE): B is [E, K, N] and the tile's rows belong to expert
+            // (mb * BM) / rows_per_group.
+            const int e = rows_per_group > 0 ? (mb * BM) / rows_per_group : -1;
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) {
-              tma_load_2d(&tmB, &full[stage], sb + j * (64 * BK * 2), nb * BN + j * 64, kb * BK);
+              if (e < 0) {
+                tma_load_2d(&tmB, &full[stage], sb + j * (64 * BK * 2), nb * BN + j * 64, kb * BK);
+              } else {
+                tma_load_3d(&tmB, &full[stage], sb + j * (64 * BK * 2), nb * BN + j * 64, kb * BK, e);
+              }
             }
           }
           if (++stage == STAGES) {
@@ -783,9 +790,11 @@ int set_smem(Kern kernel, int bytes) {
   return set_kernel_smem(reinterpret_cast<const void*>(kernel), bytes);
 }
 
+// groups > 0 (MoE, B [K, N] layout only): B is [groups, K, N] and rows
+// [g * M / groups, (g + 1) * M / groups) of A and C use B[g].
 template <int BN, int STAGES, bool BF16, bool B_KMAJOR>
 int launch_main(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda,
-                int64_t ldb, int64_t ldc, cudaStream_t stream) {
+                int64_t ldb, int64_t ldc, cudaStream_t stream, int groups = 0) {
   using L = Layout<BN, STAGES>;
   const CUtensorMapDataType dt =
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -802,6 +811,14 @@ int launch_main(const void* A, const void* B, void* C, int M, int N, int K, int6
     const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
     const uint32_t box[2] = {BK, BN};
     int s = encode_tmap(&tb, dt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  } else if (groups > 0) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K),
+                              static_cast<uint64_t>(groups)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ldb) * 2,
+                                 static_cast<uint64_t>(ldb) * 2 * static_cast<uint64_t>(K)};
+    const uint32_t box[3] = {64, BK, 1};
+    int s = encode_tmap(&tb, dt, 3, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != KTA_OK) return s;
   } else {
     const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
@@ -823,7 +840,9 @@ int launch_main(const void* A, const void* B, void* C, int M, int N, int K, int6
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int sms = current_sm_count();
   const int grid = std::max(1, std::min(tiles, sms));
-  kernel<<<grid, NUM_THREADS, L::ALLOC, stream>>>(ta, tb, tc, M, N, K, device_status_ptr());
+  const int rows_per_group = groups > 0 ? M / groups : 0;
+  kernel<<<grid, NUM_THREADS, L::ALLOC, stream>>>(ta, tb, tc, M, N, K, rows_per_group,
+                                                   device_status_ptr());
   return launch_status();
 }
 
@@ -1011,8 +1030,50 @@ int dispatch(const void* A, const void* B, void* C, int64_t M64, int64_t N64, in
   return launch_main<64, 8, BF16, B_KMAJOR>(A, B, C, M, N, K, lda, ldb, ldc, stream);
 }
 
+// MoE expert GEMM (KTA's moe_gemm, perfmodel/testset/gen.py:332-356): tokens grouped by
+// expert, T / E rows each (a multiple of the 128-row tile, so no tile straddles two
+// experts), C[rows of e] = A[rows of e] . W[e] with W [E, K, N]. One persistent launch over
+// all experts' tiles; the producer picks W[e] per tile through a 3-D tensor map.
+template <bool BF16>
+int moe_dispatch(const void* A, const void* W, void* C, int64_t E64, int64_t T64, int64_t N64,
+                 int64_t K64, void* stream_v) {
+  if (A == nullptr || W == nullptr || C == nullptr) return KTA_ERR_INVALID_ARG;
+  if (E64 <= 0 || T64 <= 0 || N64 <= 0 || K64 <= 0) return KTA_ERR_INVALID_ARG;
+  if (E64 > 65536 || T64 > (1 << 30) || N64 > (1 << 30) || K64 > (1 << 30)) {
+    return KTA_ERR_UNSUPPORTED;
+  }
+  if (T64 % E64 != 0 || (T64 / E64) % BM != 0) return KTA_ERR_UNSUPPORTED;
+  if (!aligned16(A) || !aligned16(W) || !aligned16(C)) return KTA_ERR_ALIGN;
+  if (K64 % 8 || N64 % 8) return KTA_ERR_ALIGN;
+  int s = require_sm100();
+  if (s != KTA_OK) return s;
+  const int E = static_cast<int>(E64), T = static_cast<int>(T64), N = static_cast<int>(N64),
+            K = static_cast<int>(K64);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  const int sms = std::max(1, current_sm_count());
+  if (tile_cost(T, N, 256, sms) <= tile_cost(T, N, 128, sms)) {
+    return launch_main<256, 4, BF16, false>(A, W, C, T, N, K, K, N, N, stream, E);
+  }
+  return launch_main<128, 6, BF16, false>(A, W, C, T, N, K, K, N, N, stream, E);
+}
+
 }  // namespace gemm
 }  // namespace kta
+
+extern "C" int kta_moe_gemm_f16(const void* A, const void* W, void* C, int64_t E, int64_t T,
+                                int64_t N, int64_t K, void* stream) {
+  return kta::gemm::moe_dispatch<false>(A, W, C, E, T, N, K, stream);
+}
+extern "C" int kta_moe_gemm_bf16(const void* A, const void* W, void* C, int64_t E, int64_t T,
+                                 int64_t N, int64_t K, void* stream) {
+  return kta::gemm::moe_dispatch<true>(A, W, C, E, T, N, K, stream);
+}
+extern "C" void kta_so_moe_gemm_f16(uint64_t A, uint64_t W, uint64_t C, int32_t E, int32_t T,
+                                    int32_t N, int32_t K) {
+  kta::set_last_error(kta_moe_gemm_f16(reinterpret_cast<const void*>(A),
+                                       reinterpret_cast<const void*>(W),
+                                       reinterpret_cast<void*>(C), E, T, N, K, nullptr));
+}
 
 extern "C" {
 

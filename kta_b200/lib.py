@@ -69,6 +69,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _ptr],
     ),
+    "kta_moe_gemm_f16": (ctypes.c_int, [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _ptr]),
+    "kta_moe_gemm_bf16": (ctypes.c_int, [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _ptr]),
+    "kta_so_moe_gemm_f16": (None, [_u64, _u64, _u64, _i32, _i32, _i32, _i32]),
     "kta_rmsnorm_f16": (ctypes.c_int, [_ptr, _ptr, _ptr, _i64, _i64, _f32, _ptr]),
     "kta_rmsnorm_bf16": (ctypes.c_int, [_ptr, _ptr, _ptr, _i64, _i64, _f32, _ptr]),
     "kta_softmax_f16": (ctypes.c_int, [_ptr, _ptr, _i64, _i64, _ptr]),

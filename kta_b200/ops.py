@@ -95,6 +95,25 @@ def gemm_fp8_blockscaled(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb:
     return out
 
 
+def moe_gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """MoE expert GEMM: A [T, K] with tokens grouped by expert (T / E rows each, a multiple
+    of 128), W [E, K, N]; C[rows of e] = A[rows of e] @ W[e]; f16 or bf16, fp32 accumulate."""
+    _need_cuda(a, w)
+    if a.dim() != 2 or w.dim() != 3 or a.shape[1] != w.shape[1]:
+        raise ValueError("A must be [T, K] and W [E, K, N]")
+    if a.dtype != w.dtype or a.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("A and W must share an f16 or bf16 dtype")
+    if not a.is_contiguous() or not w.is_contiguous():
+        raise ValueError("A and W must be contiguous")
+    t, k = a.shape
+    e, _, n = w.shape
+    if out is None:
+        out = torch.empty((t, n), dtype=a.dtype, device=a.device)
+    entry = "kta_moe_gemm_f16" if a.dtype == torch.float16 else "kta_moe_gemm_bf16"
+    lib.call(entry, a.data_ptr(), w.data_ptr(), out.data_ptr(), e, t, n, k, _stream())
+    return out
+
+
 def _rowop_check(x: torch.Tensor, name: str) -> None:
     if x.dim() != 2 or not x.is_contiguous():
         raise ValueError(f"{name} must be a contiguous [M, N] tensor")

@@ -44,6 +44,10 @@ def _decode(t, shape, out):
                                 out=out["O"])}
 
 
+def _moe(t, shape, out):
+    return {"C": ops.moe_gemm(t["A"], t["W"], out=out["C"])}
+
+
 def _rms(t, shape, out):
     return {"Y": ops.rmsnorm(t["X"], t["W"], eps=1e-6, out=out["Y"])}
 
@@ -53,6 +57,8 @@ def _softmax(t, shape, out):
 
 
 RUNNERS: dict[str, Callable[..., dict[str, torch.Tensor]]] = {
+    "kta_moe_gemm_f16": _moe,
+    "kta_moe_gemm_bf16": _moe,
     "kta_rmsnorm_f16": _rms,
     "kta_rmsnorm_bf16": _rms,
     "kta_softmax_f16": _softmax,

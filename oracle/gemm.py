@@ -24,3 +24,12 @@ def gemm_nn(a: np.ndarray, b: np.ndarray) -> np.ndarray:
 def gemm_tn_rows(a: np.ndarray, b: np.ndarray, rows: np.ndarray) -> np.ndarray:
     """Rows ``rows`` of A @ B.T only: full-size checks at a fraction of the FLOPs."""
     return np.asarray(a[rows], dtype=np.float64) @ np.asarray(b, dtype=np.float64).T
+
+
+def moe_gemm(a: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """MoE expert GEMM in float64 (KTA's moe_gemm, perfmodel/testset/gen.py:332-356): A [T, K]
+    with T / E consecutive rows per expert, W [E, K, N]; C[rows of e] = A[rows of e] @ W[e]."""
+    e = w.shape[0]
+    per = a.shape[0] // e
+    a64, w64 = np.asarray(a, np.float64), np.asarray(w, np.float64)
+    return np.concatenate([a64[i * per:(i + 1) * per] @ w64[i] for i in range(e)], axis=0)

@@ -292,6 +292,12 @@ def main(ref_root: str) -> int:
     st_out.update({"smax.X": xs})
     st_out.update(run("smax", case_statement("softmax_f16"), dims, {"X": xs}, ["Y"],
                       library=False))
+    dims = {"E": 3, "T": 12, "N": 20, "K": 24}
+    am = gen("A", ["T", "K"], "f16")
+    wm = gen("W", ["E", "K", "N"], "f16")
+    st_out.update({"moe.A": am, "moe.W": wm})
+    st_out.update(run("moe", case_statement("moe_gemm_f16"), dims, {"A": am, "W": wm}, ["C"],
+                      library=False))
     np.savez(HERE / "statements.npz", **st_out)
     shutil.rmtree(work_dir)
     print("wrote", sorted(p.name for p in HERE.iterdir()))

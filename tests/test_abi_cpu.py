@@ -106,6 +106,18 @@ def test_fp8_argument_checks():
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_moe_argument_checks(dt):
+    f = getattr(lib.load(), f"kta_moe_gemm_{dt}")
+    a = ALIGNED
+    assert f(a, a, a, 8, 1000, 1024, 2048, None) == 2     # T not a multiple of E
+    assert f(a, a, a, 8, 8 * 100, 1024, 2048, None) == 2  # T / E not a multiple of 128
+    assert f(a, a, a, 8, 2048, 1020, 2048, None) == 3     # N % 8
+    assert f(None, a, a, 8, 2048, 1024, 2048, None) == 1
+    assert f(a, a, a, 0, 2048, 1024, 2048, None) == 1
+    assert f(a, MISALIGNED, a, 8, 2048, 1024, 2048, None) == 3
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
 def test_rowop_argument_checks(dt):
     L = lib.load()
     rms = getattr(L, f"kta_rmsnorm_{dt}")

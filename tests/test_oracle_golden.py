@@ -128,3 +128,9 @@ def test_softmax_matches_reference_statement_runner(st):
     x = st["smax.X"]
     np.testing.assert_allclose(rowops.softmax(x), st["smax.Y.f64"].reshape(x.shape),
                                rtol=1e-12, atol=1e-15)
+
+
+def test_moe_matches_reference_statement_runner(st):
+    a, w = st["moe.A"], st["moe.W"]
+    ref = st["moe.C.f64"].reshape(a.shape[0], w.shape[2])
+    np.testing.assert_allclose(ogemm.moe_gemm(a, w), ref, rtol=1e-12, atol=1e-12)
