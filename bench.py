@@ -7,11 +7,12 @@ on the data path; the total work is fixed as N grows ("scaling": "strong").
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kta|reference]
                     [--workload gemm_bf16_8192|gemm_bf16_skinny|gemm_f16_1024|attn_causal|
-                                decode_gqa|gemm_fp8]
+                                decode_gqa|gemm_fp8|moe_gemm_f16|rmsnorm_f16|softmax_f16|
+                                w4gemm_f16|nvfp4gemm_f16]
 
 A step is one launch of the hot-path kernel over one rotating input set already resident in
-HBM (4 sets; every workload's inputs exceed the 126 MB L2, so no flush is needed between
-steps). Rank 0 prints one JSON line: the driver's keys plus `roofline` (the dominant kernel's
+HBM (at least 4 sets, and as many as make the sets together twice the 126 MB L2, so no flush
+is needed between steps). Rank 0 prints one JSON line: the driver's keys plus `roofline` (the dominant kernel's
 achieved rate from CUDA events against MEASURED_PEAKS.json), `sol` (the case's L1
 speed-of-light bound, as KTA reports pct_of_bound), `e2e` (the same metric through the
 public API with pinned host inputs copied in and the result copied out every step),
@@ -36,6 +37,7 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parent
@@ -43,6 +45,16 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "GEMM/attention TFLOP/s (decode: HBM GB/s) & % of SOL at 1/2/4/8 B200"
 NSETS = int(os.environ.get("KTA_BENCH_SETS", "4"))  # rotating input sets (1 for ncu captures)
+L2_BYTES = 126 * 1000 * 1000
+
+
+def sets_for(bytes_per_set: float) -> int:
+    """Rotating input sets: NSETS, raised until the sets together are twice the L2, so a step
+    never finds its inputs left in L2 by the previous steps; KTA_BENCH_SETS set explicitly (a
+    small ncu capture) wins."""
+    if "KTA_BENCH_SETS" in os.environ:
+        return NSETS
+    return max(NSETS, int(-(-2 * L2_BYTES // max(int(bytes_per_set), 1))))
 CPU_BUDGET_S = 12.0  # CPU baseline sample: about this much host compute
 
 
@@ -226,6 +238,7 @@ class GemmWorkload:
         self.dtype_name = "bf16" if dtype == torch.bfloat16 else "f16"
         # a 1024^3 GEMM runs for a few microseconds: shorter than the host's launch path
         self.graph_default = 2.0 * m * n * k < 2e10
+        self.nsets = sets_for((m * k + self.n * k + m * self.n) * self.esize)
 
     @property
     def flops(self) -> float:
@@ -249,22 +262,22 @@ class GemmWorkload:
             "M": self.m, "N": self.n_total, "K": self.k,
             "global_batch": self.m, "seq_len": None,
             "parallelism": f"N-column shards x{world} (no collective)",
-            "l2": "inputs larger than L2 (126 MB): 4 rotating input sets, no flush",
+            "l2": f"inputs larger than L2 (126 MB): {self.nsets} rotating input sets, no flush",
             "inputs": "N(0,1)/sqrt(K) from a seeded torch generator",
         }
 
     def setup(self, device: torch.device) -> None:
         g = torch.Generator(device=device).manual_seed(1234)
         s = 1.0 / math.sqrt(self.k)
-        self.a = [_randn((self.m, self.k), self.dtype, g, s) for _ in range(NSETS)]
-        self.b = [_randn((self.n, self.k), self.dtype, g, s) for _ in range(NSETS)]
+        self.a = [_randn((self.m, self.k), self.dtype, g, s) for _ in range(self.nsets)]
+        self.b = [_randn((self.n, self.k), self.dtype, g, s) for _ in range(self.nsets)]
         self.c = [torch.empty((self.m, self.n), dtype=self.dtype, device=device)
-                  for _ in range(NSETS)]
+                  for _ in range(self.nsets)]
 
     def launch(self, i: int) -> None:
         from kta_b200 import ops
 
-        j = i % NSETS
+        j = i % self.nsets
         ops.gemm(self.a[j], self.b[j], out=self.c[j])
 
     # ---- end to end: pinned host inputs in, result out, every step ----
@@ -681,6 +694,7 @@ class MoeWorkload:
         self.e = max(hi - lo, 0)
         self.t = self.e * (t // e)
         self.m = self.t
+        self.nsets = sets_for((self.t * k + self.e * k * n + self.t * n) * 2)
 
     @property
     def flops(self) -> float:
@@ -702,21 +716,22 @@ class MoeWorkload:
                 "case": self.case, "E": self.e_total, "T": self.t_total, "N": self.n,
                 "K": self.k, "global_batch": self.t_total, "seq_len": None,
                 "parallelism": f"expert shards x{world} (no collective)",
-                "l2": "4 rotating input sets of 25 MB (L2-resident: the test set's warm case)",
+                "l2": f"inputs larger than L2 together: {self.nsets} rotating input sets",
                 "inputs": "N(0,1)/sqrt(K) f16 from a seeded torch generator"}
 
     def setup(self, device: torch.device) -> None:
         g = torch.Generator(device=device).manual_seed(2468)
         s = 1.0 / math.sqrt(self.k)
-        self.a = [_randn((self.t, self.k), torch.float16, g, s) for _ in range(NSETS)]
-        self.w = [_randn((self.e, self.k, self.n), torch.float16, g, s) for _ in range(NSETS)]
+        self.a = [_randn((self.t, self.k), torch.float16, g, s) for _ in range(self.nsets)]
+        self.w = [_randn((self.e, self.k, self.n), torch.float16, g, s)
+                  for _ in range(self.nsets)]
         self.c = [torch.empty((self.t, self.n), dtype=torch.float16, device=device)
-                  for _ in range(NSETS)]
+                  for _ in range(self.nsets)]
 
     def launch(self, i: int) -> None:
         from kta_b200 import ops
 
-        j = i % NSETS
+        j = i % self.nsets
         ops.moe_gemm(self.a[j], self.w[j], out=self.c[j])
 
     def setup_e2e(self, device: torch.device) -> None:
@@ -755,6 +770,117 @@ class MoeWorkload:
         units = 2.0 * rows * self.n * self.k
         return run, units, (f"one expert's A @ W[e] in f16 on the host, {rows} of its {per} "
                             f"rows, N={self.n}, K={self.k}")
+
+
+class Dq4Workload:
+    """GEMM with a 4-bit B dequantised in the main loop (KTA's test-set w4gemm, group 32, and
+    nvfp4gemm, e2m1 with 16-element blocks; perfmodel/testset/gen.py:359-414, :744-778) at the
+    test set's M=N=K=2048, f16 A, scales and C; this rank's N-column shard of B."""
+
+    kernel_regex = "dq_gemm_kernel"
+    unit = "TFLOP/s"
+    dtype_name = "f16"
+    graph_default = True  # ~20 us per launch: near the host launch path
+
+    def __init__(self, fmt: str, dist: Dist, m: int = 2048, n: int = 2048,
+                 k: int = 2048) -> None:
+        self.fmt = fmt
+        self.group = 32 if fmt == "int4" else 16
+        self.case = "w4gemm_f16" if fmt == "int4" else "nvfp4gemm_f16"
+        self.m, self.n_total, self.k = m, n, k
+        lo, hi = shard(n, dist.world, dist.rank, align=128)
+        self.n0, self.n = lo, hi - lo
+        self.nsets = sets_for(2 * m * k + self.n * k // 2 + 2 * self.n * (k // self.group)
+                              + 2 * m * self.n)
+
+    @property
+    def flops(self) -> float:
+        return 2.0 * self.m * self.n * self.k
+
+    @property
+    def bytes(self) -> float:
+        return float(2 * self.m * self.k + self.n * self.k // 2
+                     + 2 * self.n * (self.k // self.group) + 2 * self.m * self.n)
+
+    def work(self) -> float:
+        return self.flops
+
+    def sol_shape(self) -> dict:
+        return {"M": self.m, "N": self.n, "K": self.k}
+
+    def config(self, world: int) -> dict:
+        what = ("w4a16: B = (nibble - 8) * scale per 32 along K" if self.fmt == "int4"
+                else "NVFP4: B = e2m1(nibble) * scale per 16 along K")
+        return {"workload": f"{self.case}: M={self.m} N={self.n_total} K={self.k}, {what}, "
+                            "f16 A / scales / C, fp32 accumulate",
+                "case": self.case, "M": self.m, "N": self.n_total, "K": self.k,
+                "global_batch": self.m, "seq_len": None,
+                "parallelism": f"N-column shards x{world} (no collective)",
+                "l2": f"inputs larger than L2 together: {self.nsets} rotating input sets",
+                "inputs": "A N(0,1)/sqrt(K) f16 (seeded torch); B N(0,1) quantised on the host"}
+
+    def _quantised(self, n: int, seed: int):
+        from kta_b200.inputs import quantize_4bit
+
+        src = np.random.default_rng(seed).standard_normal((n, self.k)).astype(np.float32)
+        bq, sc = quantize_4bit(src, self.fmt, self.group)
+        return torch.from_numpy(bq), torch.from_numpy(sc)
+
+    def setup(self, device: torch.device) -> None:
+        g = torch.Generator(device=device).manual_seed(1357)
+        s = 1.0 / math.sqrt(self.k)
+        hbq, hsc = self._quantised(self.n, 11)
+        self.sets = [(_randn((self.m, self.k), torch.float16, g, s), hbq.to(device),
+                      hsc.to(device)) for _ in range(self.nsets)]
+        self.c = [torch.empty((self.m, self.n), dtype=torch.float16, device=device)
+                  for _ in range(self.nsets)]
+
+    def launch(self, i: int) -> None:
+        from kta_b200 import ops
+
+        j = i % self.nsets
+        ops.gemm_4bit(*self.sets[j], self.fmt, self.group, out=self.c[j])
+
+    def setup_e2e(self, device: torch.device) -> None:
+        g = torch.Generator().manual_seed(99)
+        self.ha = _randn((self.m, self.k), torch.float16, g, 1.0 / math.sqrt(self.k),
+                         device="cpu").pin_memory()
+        bq, sc = self._quantised(self.n, 12)
+        self.hbq, self.hsc = bq.pin_memory(), sc.pin_memory()
+        self.hc = torch.empty((self.m, self.n), dtype=torch.float16).pin_memory()
+        self.da, self.dbq, self.dsc, self.dc = (torch.empty_like(t, device=device)
+                                                for t in (self.ha, self.hbq, self.hsc, self.hc))
+        self.h2d_bytes = self.ha.numel() * 2 + self.hbq.numel() + self.hsc.numel() * 2
+        self.d2h_bytes = self.hc.numel() * 2
+
+    def e2e_step(self) -> None:
+        from kta_b200 import ops
+
+        self.da.copy_(self.ha, non_blocking=True)
+        self.dbq.copy_(self.hbq, non_blocking=True)
+        self.dsc.copy_(self.hsc, non_blocking=True)
+        ops.gemm_4bit(self.da, self.dbq, self.dsc, self.fmt, self.group, out=self.dc)
+        self.hc.copy_(self.dc, non_blocking=True)
+
+    def cpu_sample(self, rows: int):
+        """The case statement (unpack, dequantise in f16, multiply) on the host for `rows`
+        rows of A against the whole B."""
+        rows = max(1, min(rows, self.m))
+        g = torch.Generator().manual_seed(7)
+        a = _randn((rows, self.k), torch.float16, g, 1.0 / math.sqrt(self.k), device="cpu")
+        bq, sc = self._quantised(self.n_total, 13)
+
+        def run():
+            from kta_b200 import schemas
+            from oracle import statement
+
+            stmt = schemas.load_case_file(self.case).problem.reference_impl
+            statement.run_library(stmt, {"A": a, "Bq": bq, "Sc": sc},
+                                  {"M": rows, "N": self.n_total, "K": self.k}, ["C"])
+
+        units = 2.0 * rows * self.n_total * self.k
+        return run, units, (f"{self.case} statement in f16 on the host, M={rows} rows (of "
+                            f"{self.m}), N={self.n_total}, K={self.k}")
 
 
 class RowOpWorkload:
@@ -864,6 +990,8 @@ WORKLOADS = {
     "moe_gemm_f16": lambda d: MoeWorkload(d),
     "rmsnorm_f16": lambda d: RowOpWorkload("rmsnorm", d),
     "softmax_f16": lambda d: RowOpWorkload("softmax", d),
+    "w4gemm_f16": lambda d: Dq4Workload("int4", d),
+    "nvfp4gemm_f16": lambda d: Dq4Workload("e2m1", d),
 }
 
 

@@ -132,6 +132,18 @@ int kta_decode_gqa_bf16_noalloc(const void* Q, const void* Kc, const void* Vc,
                                 int64_t Hq, int64_t Hkv, int64_t D, int64_t cache_tokens,
                                 int64_t max_seqlen, float scale, void* stream);
 
+/* GEMM with a 4-bit B dequantised in the main loop: C [M, N] f16 = A [M, K] f16 . B^T with
+ * B[n, k] = decode(nibble k of Bq[n, :]) * Sc[n, k / group] rounded to f16; Bq [N, K/2] bytes,
+ * two elements per byte, the lower nibble first; Sc [N, K/group] f16; fp32 accumulate.
+ *   w4a16: decode(x) = x - 8, group a power of two >= 16 (KTA's w4gemm,
+ *          perfmodel/testset/gen.py:359-414, group 32 there);
+ *   NVFP4: decode = the e2m1 value, group 16 (KTA's nvfp4gemm, gen.py:744-778).
+ * K % 64 == 0, K % group == 0, N % 8 == 0; 16-byte aligned A, Bq, C, 2-byte aligned Sc. */
+int kta_gemm_w4a16_f16(const void* A, const void* Bq, const void* Sc, void* C, int64_t M,
+                       int64_t N, int64_t K, int64_t group, void* stream);
+int kta_gemm_nvfp4_f16(const void* A, const void* Bq, const void* Sc, void* C, int64_t M,
+                       int64_t N, int64_t K, void* stream);
+
 /* MoE expert GEMM: tokens grouped by expert, T / E rows each; for every expert e,
  * C[e*T/E : (e+1)*T/E, :] = A[e*T/E : (e+1)*T/E, :] . W[e] with A [T, K], W [E, K, N] and C
  * [T, N] row-major f16 or bf16, fp32 accumulate. Replaces KTA's test-set moe_gemm
@@ -169,6 +181,11 @@ void kta_so_gemm_nn_bf16(uint64_t A, uint64_t B, uint64_t C, int32_t M, int32_t 
 /* the test set's rmsnorm (eps 1e-6) and softmax, f16, with its (X, W, Y, M, N) / (X, Y, M, N)
  * parameters (perfmodel/testset/gen.py:662-704, :781-807) */
 void kta_so_rmsnorm_f16(uint64_t X, uint64_t W, uint64_t Y, int32_t M, int32_t N);
+/* the test set's w4gemm (group 32) and nvfp4gemm, with their (A, Bq, Sc, C) tensors */
+void kta_so_w4gemm_f16(uint64_t A, uint64_t Bq, uint64_t Sc, uint64_t C, int32_t M, int32_t N,
+                       int32_t K);
+void kta_so_nvfp4gemm_f16(uint64_t A, uint64_t Bq, uint64_t Sc, uint64_t C, int32_t M, int32_t N,
+                          int32_t K);
 /* the test set's moe_gemm, f16, with its (A, W, C) tensors and (E, T, N, K) sizes */
 void kta_so_moe_gemm_f16(uint64_t A, uint64_t W, uint64_t C, int32_t E, int32_t T, int32_t N,
                          int32_t K);

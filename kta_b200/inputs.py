@@ -48,6 +48,8 @@ DTYPES: dict[str, Any] = {
     "int32": np.int32,
     "i64": np.int64,
     "int64": np.int64,
+    "i8": np.int8,
+    "int8": np.int8,
 }
 ITEMSIZE = {k: np.dtype(v).itemsize for k, v in DTYPES.items()}
 EXTREME_SCALE = {"f16": 16.0, "float16": 16.0, "bf16": 16.0, "bfloat16": 16.0,
@@ -207,6 +209,37 @@ def quantize_blockwise_e4m3(x: np.ndarray, block_rows: int, block_cols: int = 12
     return codes.view(torch.uint8).numpy().copy(), scale
 
 
+# ---- 4-bit weights (w4a16 int4, NVFP4 e2m1) ------------------------------------------------
+
+E2M1_GRID = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+
+
+def quantize_4bit(x: np.ndarray, fmt: str, group: int) -> tuple[np.ndarray, np.ndarray]:
+    """Packed 4-bit codes (int8 [N, K/2], two per byte, the lower nibble first) and f16 scales
+    [N, K/group] of a 2-D float array. int4: scale = amax / 7 (f16), code = round(x / scale) + 8
+    clipped to [0, 15] (value = code - 8); e2m1: scale = amax / 6 (f16), code = the nearest e2m1
+    magnitude's index, sign in bit 3. An all-zero group gets scale 1."""
+    x = np.asarray(x, dtype=np.float32)
+    n, k = x.shape
+    if k % group or k % 2:
+        raise NotSupported(f"K={k} must be a multiple of the group ({group}) and of 2")
+    blocks = x.reshape(n, k // group, group)
+    amax = np.abs(blocks).max(axis=-1)
+    top = 7.0 if fmt == "int4" else 6.0
+    scale = np.where(amax > 0, amax / top, 1.0).astype(np.float16)
+    y = blocks / scale.astype(np.float32)[..., None]
+    if fmt == "int4":
+        codes = np.clip(np.rint(y) + 8, 0, 15).astype(np.uint8)
+    elif fmt == "e2m1":
+        idx = np.abs(np.abs(y)[..., None] - E2M1_GRID).argmin(axis=-1).astype(np.uint8)
+        codes = idx | np.where(y < 0, np.uint8(8), np.uint8(0))
+    else:
+        raise NotSupported(f"4-bit format {fmt!r}")
+    codes = codes.reshape(n, k)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+    return packed.view(np.int8), scale
+
+
 # ---- whole input sets of a case -----------------------------------------------------------
 
 def case_inputs(problem, shape: dict[str, Any], dist: str, rng: random.Random,
@@ -219,7 +252,9 @@ def case_inputs(problem, shape: dict[str, Any], dist: str, rng: random.Random,
     ``lengths`` {low, high, seqlens, offsets, total} draws per-sequence lengths uniform in
     [low, high] (clipped to max_seqlen), packs them back to back and sets the total as a
     shape variable; ``quantize`` {tensor: {scale, block}} draws the tensor's source values
-    from ``dist`` and stores e4m3 codes plus fp32 block scales amax/448."""
+    from ``dist`` and stores e4m3 codes plus fp32 block scales amax/448; ``pack4`` {tensor,
+    scale, format, group} draws [N, K] source values and stores packed 4-bit codes plus f16
+    group scales (``quantize_4bit``)."""
     shape = dict(shape)
     out: dict[str, np.ndarray] = {}
     lengths = problem.params.get("lengths")
@@ -234,6 +269,14 @@ def case_inputs(problem, shape: dict[str, Any], dist: str, rng: random.Random,
         out[lengths["offsets"]] = off
     quant = problem.params.get("quantize") or {}
     scale_of = {v["scale"]: k for k, v in quant.items()}
+    pack4 = problem.params.get("pack4")
+    if pack4:
+        # the packed tensor's source values are [N, K] (the packed shape is [N, K/2])
+        spec = TensorSpec(name=pack4["tensor"], shape=["N", "K"], dtype="f32",
+                          layout="row_major")
+        src = generate(spec, shape, dist, rng, table).astype(np.float32)
+        out[pack4["tensor"]], out[pack4["scale"]] = quantize_4bit(
+            src, pack4["format"], int(pack4["group"]))
     for t in problem.inputs:
         if t.name in out:
             continue

@@ -69,6 +69,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _ptr],
     ),
+    "kta_gemm_w4a16_f16": (ctypes.c_int,
+                           [_ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _ptr]),
+    "kta_gemm_nvfp4_f16": (ctypes.c_int, [_ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _ptr]),
+    "kta_so_w4gemm_f16": (None, [_u64, _u64, _u64, _u64, _i32, _i32, _i32]),
+    "kta_so_nvfp4gemm_f16": (None, [_u64, _u64, _u64, _u64, _i32, _i32, _i32]),
     "kta_moe_gemm_f16": (ctypes.c_int, [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _ptr]),
     "kta_moe_gemm_bf16": (ctypes.c_int, [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _ptr]),
     "kta_so_moe_gemm_f16": (None, [_u64, _u64, _u64, _i32, _i32, _i32, _i32]),

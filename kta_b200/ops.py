@@ -95,6 +95,38 @@ def gemm_fp8_blockscaled(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb:
     return out
 
 
+def gemm_4bit(a: torch.Tensor, bq: torch.Tensor, sc: torch.Tensor, fmt: str = "int4",
+              group: int = 32, out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = A @ B^T with B dequantised from 4-bit codes: A f16 [M, K]; Bq int8/uint8 [N, K/2]
+    (two codes per byte, the lower nibble first); Sc f16 [N, K/group]. ``fmt`` "int4"
+    (value = code - 8, any power-of-two group >= 16) or "e2m1" (NVFP4, group 16)."""
+    _need_cuda(a, bq, sc)
+    if a.dtype != torch.float16 or sc.dtype != torch.float16:
+        raise ValueError("A and Sc must be f16")
+    if bq.dtype not in (torch.int8, torch.uint8):
+        raise ValueError("Bq must be int8 or uint8 bytes")
+    for t, name in ((a, "A"), (bq, "Bq"), (sc, "Sc")):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    m, k = a.shape
+    n = bq.shape[0]
+    if bq.shape != (n, k // 2) or sc.shape != (n, k // group):
+        raise ValueError("Bq must be [N, K/2] and Sc [N, K/group]")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16, device=a.device)
+    if fmt == "int4":
+        lib.call("kta_gemm_w4a16_f16", a.data_ptr(), bq.data_ptr(), sc.data_ptr(),
+                 out.data_ptr(), m, n, k, group, _stream())
+    elif fmt == "e2m1":
+        if group != 16:
+            raise ValueError("NVFP4 scales one block of 16 elements")
+        lib.call("kta_gemm_nvfp4_f16", a.data_ptr(), bq.data_ptr(), sc.data_ptr(),
+                 out.data_ptr(), m, n, k, _stream())
+    else:
+        raise ValueError(f"unknown 4-bit format {fmt!r}")
+    return out
+
+
 def moe_gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """MoE expert GEMM: A [T, K] with tokens grouped by expert (T / E rows each, a multiple
     of 128), W [E, K, N]; C[rows of e] = A[rows of e] @ W[e]; f16 or bf16, fp32 accumulate."""

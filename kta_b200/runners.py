@@ -44,6 +44,14 @@ def _decode(t, shape, out):
                                 out=out["O"])}
 
 
+def _w4(t, shape, out):
+    return {"C": ops.gemm_4bit(t["A"], t["Bq"], t["Sc"], "int4", 32, out=out["C"])}
+
+
+def _nvfp4(t, shape, out):
+    return {"C": ops.gemm_4bit(t["A"], t["Bq"], t["Sc"], "e2m1", 16, out=out["C"])}
+
+
 def _moe(t, shape, out):
     return {"C": ops.moe_gemm(t["A"], t["W"], out=out["C"])}
 
@@ -57,6 +65,8 @@ def _softmax(t, shape, out):
 
 
 RUNNERS: dict[str, Callable[..., dict[str, torch.Tensor]]] = {
+    "kta_gemm_w4a16_f16": _w4,
+    "kta_gemm_nvfp4_f16": _nvfp4,
     "kta_moe_gemm_f16": _moe,
     "kta_moe_gemm_bf16": _moe,
     "kta_rmsnorm_f16": _rms,
@@ -73,7 +83,8 @@ RUNNERS: dict[str, Callable[..., dict[str, torch.Tensor]]] = {
 }
 
 _TORCH = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32,
-          "e4m3": torch.float8_e4m3fn, "i32": torch.int32, "i64": torch.int64}
+          "e4m3": torch.float8_e4m3fn, "i32": torch.int32, "i64": torch.int64,
+          "i8": torch.int8}
 
 
 def run(entry: str, problem: Problem, shape: dict[str, Any], data: dict[str, np.ndarray],

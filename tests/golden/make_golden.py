@@ -298,6 +298,18 @@ def main(ref_root: str) -> int:
     st_out.update({"moe.A": am, "moe.W": wm})
     st_out.update(run("moe", case_statement("moe_gemm_f16"), dims, {"A": am, "W": wm}, ["C"],
                       library=False))
+    sys.path.insert(0, str(REPO))
+    from kta_b200.inputs import quantize_4bit
+
+    dims = {"M": 6, "N": 10, "K": 64}
+    a4 = gen("A", ["M", "K"], "f16")
+    src = gen("Bsrc", ["N", "K"], "f32")
+    for tag, fmt, grp, case in (("w4", "int4", 32, "w4gemm_f16"),
+                                ("nvfp4", "e2m1", 16, "nvfp4gemm_f16")):
+        bq, sc = quantize_4bit(src, fmt, grp)
+        st_out.update({f"{tag}.A": a4, f"{tag}.Bq": bq, f"{tag}.Sc": sc})
+        st_out.update(run(tag, case_statement(case), dims, {"A": a4, "Bq": bq, "Sc": sc}, ["C"],
+                          library=False))
     np.savez(HERE / "statements.npz", **st_out)
     shutil.rmtree(work_dir)
     print("wrote", sorted(p.name for p in HERE.iterdir()))

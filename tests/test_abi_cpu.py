@@ -105,6 +105,19 @@ def test_fp8_argument_checks():
     assert L.kta_gemm_fp8_blockscaled(*a, 0, 128, 128, None) == 1
 
 
+def test_4bit_gemm_argument_checks():
+    L = lib.load()
+    a = ALIGNED
+    w4, nv = L.kta_gemm_w4a16_f16, L.kta_gemm_nvfp4_f16
+    assert w4(a, a, a, a, 128, 128, 100, 32, None) == 3     # K % 64
+    assert w4(a, a, a, a, 128, 128, 128, 48, None) == 1     # group not a power of two
+    assert w4(a, a, a, a, 128, 128, 192, 128, None) == 3    # K % group
+    assert w4(a, a, a, a, 128, 100, 128, 32, None) == 3     # N % 8
+    assert w4(None, a, a, a, 128, 128, 128, 32, None) == 1
+    assert nv(a, a, a, a, 0, 128, 128, None) == 1
+    assert nv(a, MISALIGNED, a, a, 128, 128, 128, None) == 3
+
+
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 def test_moe_argument_checks(dt):
     f = getattr(lib.load(), f"kta_moe_gemm_{dt}")

@@ -134,3 +134,25 @@ def test_moe_matches_reference_statement_runner(st):
     a, w = st["moe.A"], st["moe.W"]
     ref = st["moe.C.f64"].reshape(a.shape[0], w.shape[2])
     np.testing.assert_allclose(ogemm.moe_gemm(a, w), ref, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("tag,fmt,group", [("w4", "int4", 32), ("nvfp4", "e2m1", 16)])
+def test_4bit_gemm_matches_reference_statement_runner(st, tag, fmt, group):
+    """The statement runs in FP64 (B's product unrounded); the oracle rounds B to f16 as the
+    reference's kernel does: equal within f16 rounding of B."""
+    from oracle import dequant
+
+    a, bq, sc = st[f"{tag}.A"], st[f"{tag}.Bq"], st[f"{tag}.Sc"]
+    ref = st[f"{tag}.C.f64"].reshape(a.shape[0], bq.shape[0])
+    got = dequant.gemm(a, bq, sc, fmt, group)
+    assert np.linalg.norm(got - ref) <= 1e-3 * np.linalg.norm(ref)
+    exact = a.astype(np.float64) @ (dequant.decode(dequant.unpack(bq), fmt) * np.repeat(
+        sc.astype(np.float64), group, axis=1)).T
+    np.testing.assert_allclose(exact, ref, rtol=1e-12, atol=1e-12)
+
+
+def test_e2m1_decode_is_the_e2m1_table():
+    from oracle import dequant
+
+    vals = dequant.decode(np.arange(16), "e2m1")
+    assert list(vals) == [0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.0, -0.5, -1, -1.5, -2, -3, -4, -6]
