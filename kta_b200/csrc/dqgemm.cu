@@ -7,16 +7,22 @@
 //
 // Two 4-bit elements per byte, the lower nibble first; the scale is f16 and the product is
 // rounded once to f16, as the reference computes it. The tensor cores take f16 x f16
-// (tcgen05.mma kind::f16, fp32 accumulator in TMEM), so B is expanded in shared memory:
+// (tcgen05.mma kind::f16, fp32 accumulator in TMEM) with the expanded B as the MMA's A
+// operand read from TMEM, so the product is formed transposed, D[n, m] = B[n, :] . A[m, :]:
 //
-//   * warp 0: TMA producer; per 64-deep K stage the A tile (128 x 64 f16, 128-byte swizzle)
-//     and the packed B tile (128 rows x 32 bytes), 6-stage ring;
-//   * warps 6-13: converters; each thread expands 32 elements of one B row (16 bytes in,
-//     four 16-byte swizzled chunks out) into the stage's f16 B tile, K-major with the 128-byte
-//     swizzle the MMA descriptor expects, then a proxy fence and one arrival per warp;
-//   * warp 1: TMEM owner and single-thread MMA issuer (4 MMAs of K = 16 per stage) into two
-//     accumulators of 128 columns; warps 2-5: epilogue (TMEM -> f16 -> global rows);
-//   * persistent grid, grouped raster of 128 x 128 tiles; every mbarrier wait is bounded.
+//   * warp 0: TMA producer; per 64-deep K stage the A tile (up to 256 rows x 64 f16, 128-byte
+//     swizzle; the MMA's B operand) and the packed B tile (128 rows x 32 bytes), 6 stages;
+//   * warps 6-13: converters; two per TMEM lane quarter, each thread expands 32 codes of one
+//     B row and stores them with tcgen05.st into the stage's TMEM slot (one arrival per warp);
+//   * warp 1: TMEM owner and single-thread MMA issuer, M = 128 (B rows) x N = the m tile
+//     (256, or M rounded up to 16 when one tile covers M), 4 MMAs of K = 16 per stage;
+//   * warps 2-5: epilogue; thread = one B row n: TMEM columns are m, neighbouring lanes swap
+//     halves so each stores an (n, n + 1) pair of C[m, :];
+//   * persistent grid, grouped raster of tiles; every mbarrier wait is bounded.
+//
+// Shared memory carries only the TMA writes and the tensor core's reads of A (68 KB per stage
+// of 128 x 256 x 64): the expanded B goes from registers to TMEM. Writing it to shared memory
+// instead (and reading it back as an MMA operand) makes shared-memory bandwidth the bound.
 //
 // Algorithmic work per launch: 2 M N K FLOP; bytes 2 M K + N K / 2 + 2 N K / G + 2 M N.
 #include <algorithm>
@@ -27,13 +33,21 @@
 namespace kta {
 namespace dq {
 
-constexpr int BM = 128, BN = 128, BK = 64;
+constexpr int BN = 128;      // rows of B per tile: the MMA's M, TMEM lanes
+constexpr int MT_MAX = 256;  // rows of A per tile: the MMA's N, TMEM columns of D
+constexpr int BK = 64;
 constexpr int STAGES = 6;
 constexpr int CONV_WARPS = 8;
 constexpr int EPI_WARPS = 4;
 constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS + CONV_WARPS);  // 448
 constexpr int CONV_FIRST_WARP = 2 + EPI_WARPS;
 constexpr int GROUP_M = 16;
+// TMEM: D in columns [0, 256), the expanded B of stage s in [256 + 32 s, 256 + 32 (s + 1))
+// (128 rows x 64 f16, two per 32-bit column)
+constexpr int TMEM_B_COL = MT_MAX;
+constexpr int TMEM_COLS = 512;
+static_assert(TMEM_B_COL + STAGES * (BK / 2) <= TMEM_COLS, "TMEM budget of one SM");
+static_assert(CONV_WARPS == 8, "two converter warps per TMEM lane quarter");
 
 enum : unsigned int {
   SITE_PROD = 0x701,
@@ -45,15 +59,13 @@ enum : unsigned int {
 };
 
 struct Layout {
-  static constexpr int A_BYTES = BM * BK * 2;   // 16 KB, swizzled
-  static constexpr int Q_BYTES = BN * BK / 2;   // 4 KB packed B
-  static constexpr int B_BYTES = BN * BK * 2;   // 16 KB expanded B, swizzled
+  static constexpr int A_BYTES = MT_MAX * BK * 2;  // 32 KB of A rows, swizzled
+  static constexpr int Q_BYTES = BN * BK / 2;      // 4 KB of packed B
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
-  static constexpr int OFF_Q = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_Q = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_BAR = OFF_Q + STAGES * Q_BYTES;
-  // full[S], conv[S], empty[S], tfull[2], tempty[2]
-  static constexpr int NUM_BARS = 3 * STAGES + 4;
+  // full[S], conv[S], empty[S], tfull, tempty
+  static constexpr int NUM_BARS = 3 * STAGES + 2;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int TOTAL = OFF_MISC + 16;
   static constexpr int ALLOC = TOTAL + 1024;
@@ -64,6 +76,7 @@ struct Params {
   const __half* sc;   // [N, K / G]
   __half* c;          // [M, N]
   int M, N, K, group;
+  int m_tile;         // rows of A per tile (the MMA's N)
   unsigned int* status;
 };
 
@@ -136,6 +149,12 @@ __device__ __forceinline__ uint32_t half2_bits(__half a) {
   return static_cast<uint32_t>(u) | (static_cast<uint32_t>(u) << 16);
 }
 
+// One CTA per SM; tile = 128 rows of B (n) x up to 256 rows of A (m), transposed product:
+//   D[n, m] (TMEM, fp32) += Bdq[n, k] (TMEM, f16) . A[m, k] (shared memory, f16)
+// so the expanded B never touches shared memory: the converters store it into TMEM with
+// tcgen05.st and the MMA reads it from there (A operand from TMEM), while TMA brings the
+// activation tile as the MMA's B operand. A 64-deep stage moves 32 KB of A and 4 KB of codes
+// into shared memory and 32 KB of A out to the tensor core for 128 x 256 x 64 of work.
 template <bool E2M1>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
@@ -146,7 +165,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* conv = full + STAGES;
   uint64_t* empty = conv + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
+  uint64_t* tempty = tfull + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Layout::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Layout::OFF_MISC + 4);
 
@@ -158,10 +177,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&conv[s], CONV_WARPS);
       mbar_init(&empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], EPI_WARPS);
-    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, EPI_WARPS);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -170,21 +187,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmQ);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 2 * BN);
+    tmem_alloc(tmem_holder, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int tiles_m = (p.M + BM - 1) / BM;
+  const int mt = p.m_tile;
+  const int tiles_m = (p.M + mt - 1) / mt;
   const int tiles_n = (p.N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = p.K / BK;
 
   if (warp == 0) {
-    // ---------------- TMA producer: A and packed B ----------------
+    // ---------------- TMA producer: A rows (the MMA's B operand) and packed B rows ----------
     if (lane == 0) {
+      const uint32_t bytes = static_cast<uint32_t>(mt) * BK * 2 + Layout::Q_BYTES;
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -196,9 +215,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], Layout::A_BYTES + Layout::Q_BYTES);
+          mbar_arrive_expect_tx(&full[stage], bytes);
           tma_load_2d(&tmA, &full[stage], smem + Layout::OFF_A + stage * Layout::A_BYTES,
-                      kb * BK, mb * BM);
+                      kb * BK, mb * mt);
           tma_load_2d(&tmQ, &full[stage], smem + Layout::OFF_Q + stage * Layout::Q_BYTES,
                       kb * (BK / 2), nb * BN);
           if (++stage == STAGES) {
@@ -209,20 +228,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer: M = 128 (B rows, TMEM), N = m tile (A rows, smem) ---------
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(BM, BN, 0u, 0u, 0u, 0u);  // f16 x f16, K-major
+      const uint32_t idesc = make_idesc(BN, mt, 0u, 0u, 0u, 0u);  // f16 x f16, K-major
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status, SITE_MMA_TEMPTY)) {
-          break;
-        }
+        if (!mbar_wait(tempty, acc_phase ^ 1u, abort_flag, p.status, SITE_MMA_TEMPTY)) break;
         tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, SITE_MMA_FULL) ||
               !mbar_wait(&conv[stage], phase, abort_flag, p.status, SITE_MMA_CONV)) {
@@ -230,75 +245,72 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(smem + Layout::OFF_A + stage * Layout::A_BYTES);
-          const uint32_t b0 = smem_u32(smem + Layout::OFF_B + stage * Layout::B_BYTES);
+          const uint32_t b0 = smem_u32(smem + Layout::OFF_A + stage * Layout::A_BYTES);
+          const uint32_t a0 = tmem + static_cast<uint32_t>(TMEM_B_COL + stage * (BK / 2));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            umma_f16(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024),
-                     idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_f16_tmem_a(tmem, a0 + k * 8, sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
+                            (kb > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          umma_commit(&empty[stage]);  // frees the stage's shared memory and TMEM slot
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
+        umma_commit(tfull);
+        acc_phase ^= 1u;
       }
     }
   } else if (warp < CONV_FIRST_WARP) {
-    // ---------------- epilogue: thread = output row ----------------
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    int acc = 0;
+    // ---------------- epilogue: thread = one B row n, its m values along TMEM columns ------
+    const int q = warp & 3;  // the TMEM lane quarter this warp may access
+    const int n_local = q * 32 + lane;
+    const bool odd = lane & 1;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mb, nb;
       tile_of(tile, tiles_m, tiles_n, mb, nb);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, SITE_EPI)) break;
+      if (!mbar_wait(tfull, acc_phase, abort_flag, p.status, SITE_EPI)) break;
       tc_fence_after();
-      const int m = mb * BM + row;
-      const uint32_t t = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      // lanes n (even) and n + 1 swap halves so that each stores an (n, n + 1) pair of one m
+      const int n_pair = nb * BN + (n_local & ~1);
+      const uint32_t t = tmem + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < mt; c += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t + c, r);
         tmem_ld_wait();
         reg_fence(r);
-        const int n0 = nb * BN + c;
-        if (m < p.M && n0 < p.N) {
-          uint32_t pk[16];
+        const int m0 = mb * mt + c;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const __half2 h = __floats2half2_rn(__uint_as_float(r[2 * i]),
-                                                __uint_as_float(r[2 * i + 1]));
-            pk[i] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-          __half* crow = p.c + static_cast<long long>(m) * p.N + n0;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            if (n0 + 8 * i < p.N) {
-              *reinterpret_cast<uint4*>(crow + 8 * i) =
-                  make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-            }
+        for (int i = 0; i < 16; ++i) {
+          const float mine_even = __uint_as_float(r[2 * i]);
+          const float mine_odd = __uint_as_float(r[2 * i + 1]);
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? mine_even : mine_odd, 1);
+          // even lane: row m0 + 2i, (n, n + 1); odd lane: row m0 + 2i + 1, (n - 1, n)
+          const int m = m0 + 2 * i + (odd ? 1 : 0);
+          const __half2 h = odd ? __floats2half2_rn(other, mine_odd)
+                                : __floats2half2_rn(mine_even, other);
+          if (m < p.M && n_pair < p.N) {
+            *reinterpret_cast<__half2*>(p.c + static_cast<long long>(m) * p.N + n_pair) = h;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+      if (lane == 0) mbar_arrive(tempty);
+      acc_phase ^= 1u;
     }
   } else {
-    // ---------------- converters: thread = half of one B row of the stage ----------------
-    const int ct = threadIdx.x - CONV_FIRST_WARP * 32;   // 0 .. 255
-    const int n_local = ct >> 1;                         // B row within the tile
-    const int half = ct & 1;                             // k 0-31 or 32-63 of the stage
+    // ---------------- converters: thread = half (32 codes) of one B row, into TMEM ----------
+    const int q = warp & 3;                            // TMEM lane quarter of this warp
+    const int half = (warp - CONV_FIRST_WARP) >> 2;    // codes 0-31 or 32-63 of the stage
+    const int n_local = q * 32 + lane;
     const int kgroups = p.K / p.group;
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                           static_cast<uint32_t>(TMEM_B_COL + half * (BK / 4));
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -308,33 +320,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int n = nb * BN + n_local;
       const __half* sc_row = p.sc + static_cast<long long>(min(n, p.N - 1)) * kgroups;
       for (int kb = 0; kb < num_kb; ++kb) {
-        const int k0 = kb * BK + half * 32;              // first k of this thread's 32
-        // scales of the 32 elements: one when G >= 32, two (k0 and k0 + 16) when G = 16
-        const __half s_a = __ldg(sc_row + k0 / p.group);
-        const __half s_b = __ldg(sc_row + (k0 + 16) / p.group);
+        const int k0 = kb * BK + half * 32;  // first k of this thread's 32
+        // scales of the 32 codes: one when G >= 32, two (k0 and k0 + 16) when G = 16
+        const uint32_t s2a = half2_bits(__ldg(sc_row + k0 / p.group));
+        const uint32_t s2b = half2_bits(__ldg(sc_row + (k0 + 16) / p.group));
         if (!mbar_wait(&full[stage], phase, abort_flag, p.status, SITE_CONV)) {
           ok = false;
           break;
         }
         const uint4 in = *reinterpret_cast<const uint4*>(
             smem + Layout::OFF_Q + stage * Layout::Q_BYTES + n_local * (BK / 2) + half * 16);
-        const uint32_t w[4] = {in.x, in.y, in.z, in.w};  // 8 elements each, k order
-        const uint32_t b_row = smem_u32(smem + Layout::OFF_B + stage * Layout::B_BYTES) +
-                               static_cast<uint32_t>(n_local) * 128u;
+        const uint32_t w[4] = {in.x, in.y, in.z, in.w};  // 8 codes each, k order
+        uint32_t o[16];                                   // 32 f16, k order, packed in pairs
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t s2 = half2_bits(i < 2 ? s_a : s_b);
-          uint32_t o[4];
+          uint32_t v[4];
           if constexpr (E2M1) {
-            e2m1x8_to_f16(w[i], s2, o);
+            e2m1x8_to_f16(w[i], i < 2 ? s2a : s2b, v);
           } else {
-            int4x8_to_f16(w[i], s2, o);
+            int4x8_to_f16(w[i], i < 2 ? s2a : s2b, v);
           }
-          // 16-byte chunk (half * 4 + i) of the row, 128-byte swizzle: chunk ^ (row & 7)
-          const uint32_t chunk = static_cast<uint32_t>(half * 4 + i) ^ static_cast<uint32_t>(n_local & 7);
-          st_shared_v4(b_row + (chunk << 4), o[0], o[1], o[2], o[3]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[4 * i + j] = v[j];
         }
-        fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads
+        tmem_st_32x32b_x16(t_row + static_cast<uint32_t>(stage * (BK / 2)), o);
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[stage]);
         if (++stage == STAGES) {
@@ -349,7 +360,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
@@ -369,11 +380,13 @@ int launch(const void* A, const void* Bq, const void* Sc, void* C, int64_t M64, 
   int s = require_sm100();
   if (s != KTA_OK) return s;
   const int M = static_cast<int>(M64), N = static_cast<int>(N64), K = static_cast<int>(K64);
+  // m tile = the MMA's N: 256, or M rounded up to 16 when one tile covers M
+  const int mt = M >= MT_MAX ? MT_MAX : (M + 15) / 16 * 16;
   CUtensorMap ta, tq;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
     const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
-    const uint32_t box[2] = {BK, BM};
+    const uint32_t box[2] = {BK, static_cast<uint32_t>(mt)};
     s = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box,
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != KTA_OK) return s;
@@ -393,11 +406,12 @@ int launch(const void* A, const void* Bq, const void* Sc, void* C, int64_t M64, 
   prm.N = N;
   prm.K = K;
   prm.group = static_cast<int>(group);
+  prm.m_tile = mt;
   prm.status = device_status_ptr();
   auto kernel = dq_gemm_kernel<E2M1>;
   s = set_kernel_smem(reinterpret_cast<const void*>(kernel), Layout::ALLOC);
   if (s != KTA_OK) return s;
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int tiles = ((M + mt - 1) / mt) * ((N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, current_sm_count()));
   kernel<<<grid, NUM_THREADS, Layout::ALLOC, static_cast<cudaStream_t>(stream_v)>>>(ta, tq, prm);
   return launch_status();

@@ -87,18 +87,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return done != 0;
 }
 
+// The same with acquire at cluster scope: for a phase completed by another CTA's
+// release.cluster arrivals whose shared-memory writes the waiter then consumes.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n"
+      " .reg .pred p;\n"
+      " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(done)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Waits for the phase with parity `parity` of `bar` to complete. Returns false if the wait
 // ran past kWaitTimeoutNs or if another role of the CTA already aborted (`*abort` != 0);
 // in the first case it raises `*abort` and records `site` in the status block.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           unsigned int* status, unsigned int site) {
   const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait(a, parity)) return true;
+  if ((CLUSTER ? mbar_try_wait_cluster(a, parity) : mbar_try_wait(a, parity))) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i) {
-      if (mbar_try_wait(a, parity)) return true;
+      if ((CLUSTER ? mbar_try_wait_cluster(a, parity) : mbar_try_wait(a, parity))) return true;
     }
     if (*abort) return false;
     if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
@@ -400,6 +417,69 @@ __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
+}
+
+// ---------------------------------------------------------------------------------------
+// CTA pairs (cluster of two, tcgen05 cta_group::2). No multicast loads: each CTA's TMA
+// writes its own shared memory and only the completion is counted on the leader's barrier.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank_u32() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory object in cluster rank `rank` (shared::cluster window).
+__device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void pair_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on the leader's
+// barrier (`bar_cluster` is a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster,
+                                                 void* dst, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      " .reg .pred p;\n"
+      " setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the barrier at this offset in both CTAs of the pair when every tcgen05
+// op issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n"
+      " .reg .b16 m;\n"
+      " mov.b16 m, 3;\n"
+      " tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], m;\n"
+      "}\n" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
 }
 
 }  // namespace kta

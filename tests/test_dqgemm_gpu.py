@@ -66,19 +66,22 @@ def test_test_set_shape_sampled_rows(cuda_device, fmt, group):
     _check(y[rows], ref)
 
 
+@pytest.mark.parametrize("reps", [1, 5])
 @pytest.mark.parametrize("scale", [0.25, 2.0 ** -20])
-def test_every_code_and_nibble_order(cuda_device, scale):
+def test_every_code_and_nibble_order(cuda_device, scale, reps):
     """All 16 codes in both nibble positions, with power-of-two scales (exact products; 2^-20
-    is an f16 subnormal, so the decoded values are subnormal too)."""
+    is an f16 subnormal, so the decoded values are subnormal too). A is the identity stacked
+    `reps` times: M = 64 runs the single-CTA kernel, M = 320 the CTA-pair kernel."""
     n, k = 128, 64
     codes = np.tile(np.arange(16, dtype=np.uint8), (n, k // 16))
     codes = np.roll(codes, 3, axis=1)
     bq = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8).view(np.int8)
     for fmt, group in (("int4", 32), ("e2m1", 16)):
         sc = np.full((n, k // group), scale, dtype=np.float16)
-        eye = np.eye(k, dtype=np.float16)[:, :k]
+        eye = np.tile(np.eye(k, dtype=np.float16), (reps, 1))
         y = _run(cuda_device, np.ascontiguousarray(eye), bq, sc, fmt, group)
-        np.testing.assert_array_equal(y, dequant.dequant(bq, sc, fmt, group).T)
+        np.testing.assert_array_equal(y, np.tile(dequant.dequant(bq, sc, fmt, group).T,
+                                                 (reps, 1)))
 
 
 def test_nan_fill_and_so_shims(cuda_device):
