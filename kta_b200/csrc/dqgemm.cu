@@ -37,17 +37,16 @@ constexpr int BN = 128;      // rows of B per tile: the MMA's M, TMEM lanes
 constexpr int MT_MAX = 256;  // rows of A per tile: the MMA's N, TMEM columns of D
 constexpr int BK = 64;
 constexpr int STAGES = 6;
-constexpr int CONV_WARPS = 8;
-constexpr int EPI_WARPS = 4;
-constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS + CONV_WARPS);  // 448
-constexpr int CONV_FIRST_WARP = 2 + EPI_WARPS;
+constexpr int WORK_GROUPS = 4;                       // stages being expanded at once
+constexpr int WORK_WARPS = 4 * WORK_GROUPS;           // one warp per TMEM lane quarter per group
+constexpr int NUM_THREADS = 32 * (2 + WORK_WARPS);    // 576
 constexpr int GROUP_M = 16;
 // TMEM: D in columns [0, 256), the expanded B of stage s in [256 + 32 s, 256 + 32 (s + 1))
 // (128 rows x 64 f16, two per 32-bit column)
 constexpr int TMEM_B_COL = MT_MAX;
 constexpr int TMEM_COLS = 512;
 static_assert(TMEM_B_COL + STAGES * (BK / 2) <= TMEM_COLS, "TMEM budget of one SM");
-static_assert(CONV_WARPS == 8, "two converter warps per TMEM lane quarter");
+static_assert(MT_MAX / WORK_GROUPS == 64, "each worker warp drains two 32-column loads");
 
 enum : unsigned int {
   SITE_PROD = 0x701,
@@ -174,11 +173,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], CONV_WARPS);
+      mbar_init(&conv[s], 4);  // the four warps of the stage's group
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
-    mbar_init(tempty, EPI_WARPS);
+    mbar_init(tempty, WORK_WARPS);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -263,38 +262,104 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         acc_phase ^= 1u;
       }
     }
-  } else if (warp < CONV_FIRST_WARP) {
-    // ---------------- epilogue: thread = one B row n, its m values along TMEM columns ------
-    const int q = warp & 3;  // the TMEM lane quarter this warp may access
+  } else {
+    // ---------------- workers: expand B into TMEM, then drain D at the end of each tile ------
+    // Warp w serves TMEM lane quarter q = w % 4 (the lanes a warp may access) and stage group
+    // g: the CTA's stage sequence is dealt round-robin to the WORK_GROUPS groups, so that many
+    // stages are being expanded at once; a thread expands all 64 codes of its B row n.
+    const int q = warp & 3;
+    const int g = (warp - 2) >> 2;
     const int n_local = q * 32 + lane;
     const bool odd = lane & 1;
+    const int kgroups = p.K / p.group;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    long long it_base = 0;  // index of the tile's first stage in the CTA's stage sequence
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       int mb, nb;
       tile_of(tile, tiles_m, tiles_n, mb, nb);
+      const __half* sc_row =
+          p.sc + static_cast<long long>(min(nb * BN + n_local, p.N - 1)) * kgroups;
+      // this group's first stage of the tile, and the scales of the four 16-code groups
+      int kb = static_cast<int>(((g - it_base) % WORK_GROUPS + WORK_GROUPS) % WORK_GROUPS);
+      uint32_t s2[4];
+      if (kb < num_kb) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s2[j] = half2_bits(__ldg(sc_row + (kb * BK + 16 * j) / p.group));
+      }
+      for (; kb < num_kb; kb += WORK_GROUPS) {
+        const long long it = it_base + kb;
+        const int stage = static_cast<int>(it % STAGES);
+        const uint32_t phase = static_cast<uint32_t>((it / STAGES) & 1);
+        uint32_t cur[4] = {s2[0], s2[1], s2[2], s2[3]};
+        if (kb + WORK_GROUPS < num_kb) {  // the next stage's scales, in flight meanwhile
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            s2[j] = half2_bits(__ldg(sc_row + ((kb + WORK_GROUPS) * BK + 16 * j) / p.group));
+          }
+        }
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.status, SITE_CONV)) {
+          ok = false;
+          break;
+        }
+        // the row's 32 bytes: rows r and r + 4 read their halves in opposite order, so the
+        // eight rows of a 128-byte wavefront hit distinct banks
+        const uint8_t* qrow = smem + Layout::OFF_Q + stage * Layout::Q_BYTES + n_local * (BK / 2);
+        const int sw = (n_local >> 2) & 1;
+        const uint4 u0 = *reinterpret_cast<const uint4*>(qrow + 16 * sw);
+        const uint4 u1 = *reinterpret_cast<const uint4*>(qrow + 16 * (sw ^ 1));
+        const uint4 in0 = sw ? u1 : u0;
+        const uint4 in1 = sw ? u0 : u1;
+        const uint32_t w[8] = {in0.x, in0.y, in0.z, in0.w, in1.x, in1.y, in1.z, in1.w};
+        uint32_t o[32];  // 64 f16 in k order, packed in pairs
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t v[4];
+          if constexpr (E2M1) {
+            e2m1x8_to_f16(w[i], cur[i / 2], v);
+          } else {
+            int4x8_to_f16(w[i], cur[i / 2], v);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[4 * i + j] = v[j];
+        }
+        tmem_st_32x32b_x32(t_lane + static_cast<uint32_t>(TMEM_B_COL + stage * (BK / 2)), o);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[stage]);
+      }
+      if (!ok) break;
+      it_base += num_kb;
+      // drain: this warp's 64 columns (m) of D for its 32 rows (n); lanes n (even) and n + 1
+      // swap halves so that each stores an (n, n + 1) pair of one row of C
       if (!mbar_wait(tfull, acc_phase, abort_flag, p.status, SITE_EPI)) break;
       tc_fence_after();
-      // lanes n (even) and n + 1 swap halves so that each stores an (n, n + 1) pair of one m
       const int n_pair = nb * BN + (n_local & ~1);
-      const uint32_t t = tmem + (static_cast<uint32_t>(q * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < mt; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t + c, r);
+      const int c0 = g * (MT_MAX / WORK_GROUPS);
+      if (c0 < mt) {
+        uint32_t r[2][32];
+        tmem_ld_32x32b_x32(t_lane + c0, r[0]);
+        if (c0 + 32 < mt) tmem_ld_32x32b_x32(t_lane + c0 + 32, r[1]);
         tmem_ld_wait();
-        reg_fence(r);
-        const int m0 = mb * mt + c;
+        reg_fence(r[0]);
+        reg_fence(r[1]);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float mine_even = __uint_as_float(r[2 * i]);
-          const float mine_odd = __uint_as_float(r[2 * i + 1]);
-          const float other = __shfl_xor_sync(0xffffffffu, odd ? mine_even : mine_odd, 1);
-          // even lane: row m0 + 2i, (n, n + 1); odd lane: row m0 + 2i + 1, (n - 1, n)
-          const int m = m0 + 2 * i + (odd ? 1 : 0);
-          const __half2 h = odd ? __floats2half2_rn(other, mine_odd)
-                                : __floats2half2_rn(mine_even, other);
-          if (m < p.M && n_pair < p.N) {
-            *reinterpret_cast<__half2*>(p.c + static_cast<long long>(m) * p.N + n_pair) = h;
+        for (int h = 0; h < 2; ++h) {
+          const int m0 = mb * mt + c0 + 32 * h;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float mine_even = __uint_as_float(r[h][2 * i]);
+            const float mine_odd = __uint_as_float(r[h][2 * i + 1]);
+            const float other = __shfl_xor_sync(0xffffffffu, odd ? mine_even : mine_odd, 1);
+            // even lane: row m0 + 2i, (n, n + 1); odd lane: row m0 + 2i + 1, (n - 1, n)
+            const int m = m0 + 2 * i + (odd ? 1 : 0);
+            const __half2 hv = odd ? __floats2half2_rn(other, mine_odd)
+                                   : __floats2half2_rn(mine_even, other);
+            if (c0 + 32 * h < mt && m < p.M && n_pair < p.N) {
+              *reinterpret_cast<__half2*>(p.c + static_cast<long long>(m) * p.N + n_pair) = hv;
+            }
           }
         }
       }
@@ -302,57 +367,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty);
       acc_phase ^= 1u;
-    }
-  } else {
-    // ---------------- converters: thread = half (32 codes) of one B row, into TMEM ----------
-    const int q = warp & 3;                            // TMEM lane quarter of this warp
-    const int half = (warp - CONV_FIRST_WARP) >> 2;    // codes 0-31 or 32-63 of the stage
-    const int n_local = q * 32 + lane;
-    const int kgroups = p.K / p.group;
-    const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
-                           static_cast<uint32_t>(TMEM_B_COL + half * (BK / 4));
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      int mb, nb;
-      tile_of(tile, tiles_m, tiles_n, mb, nb);
-      const int n = nb * BN + n_local;
-      const __half* sc_row = p.sc + static_cast<long long>(min(n, p.N - 1)) * kgroups;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int k0 = kb * BK + half * 32;  // first k of this thread's 32
-        // scales of the 32 codes: one when G >= 32, two (k0 and k0 + 16) when G = 16
-        const uint32_t s2a = half2_bits(__ldg(sc_row + k0 / p.group));
-        const uint32_t s2b = half2_bits(__ldg(sc_row + (k0 + 16) / p.group));
-        if (!mbar_wait(&full[stage], phase, abort_flag, p.status, SITE_CONV)) {
-          ok = false;
-          break;
-        }
-        const uint4 in = *reinterpret_cast<const uint4*>(
-            smem + Layout::OFF_Q + stage * Layout::Q_BYTES + n_local * (BK / 2) + half * 16);
-        const uint32_t w[4] = {in.x, in.y, in.z, in.w};  // 8 codes each, k order
-        uint32_t o[16];                                   // 32 f16, k order, packed in pairs
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint32_t v[4];
-          if constexpr (E2M1) {
-            e2m1x8_to_f16(w[i], i < 2 ? s2a : s2b, v);
-          } else {
-            int4x8_to_f16(w[i], i < 2 ? s2a : s2b, v);
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) o[4 * i + j] = v[j];
-        }
-        tmem_st_32x32b_x16(t_row + static_cast<uint32_t>(stage * (BK / 2)), o);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&conv[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
     }
   }
 
