@@ -10,7 +10,8 @@ reference's checker (src/kta/checks/full.py:109-224).
   each kept only when the contract's shape scope holds the kernel accountable for it
   (``in_scope``, full.py:70-87); the others are listed as out of scope.
 - anti-cheat (src/kta/checks/anticheat.py): the kernels the entry launches must all be this
-  library's (a CUPTI trace through torch.profiler stands in for the reference's nsys job);
+  library's (a CUPTI trace through torch.profiler in a fresh process stands in for the
+  reference's nsys job);
   outputs are NaN-filled before the launch, so an unwritten element fails numeric; a second
   run of the same inputs must give the same bytes (determinism); the library must link none
   of the forbidden libraries (ELF dynamic section).
@@ -120,9 +121,8 @@ def _anticheat(cf: CaseFile, entry: str, shape: dict[str, Any], seed: int) -> di
     failures: list[dict[str, Any]] = []
     rng = kinp.named_rng(seed, f"checks.anticheat:{checks.canonical_json(shape)}")
     full_shape, data = kinp.case_inputs(cf.problem, shape, "normal", rng)
-    names: list[str] = []
-    first = runners.run(entry, cf.problem, full_shape, data, nan_fill=True, raw=True,
-                        launched=names)
+    names = runners.trace_kernels(entry, cf.problem, full_shape, data)
+    first = runners.run(entry, cf.problem, full_shape, data, nan_fill=True, raw=True)
     foreign = sorted({n for n in names if not any(k in n for k in KERNEL_PREFIXES)})
     if not names:
         failures.append({"check": "anticheat.kernels", "detail": "no kernel launched"})

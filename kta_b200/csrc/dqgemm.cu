@@ -143,11 +143,6 @@ __device__ __forceinline__ void e2m1x8_to_f16(uint32_t w, uint32_t s2, uint32_t 
   }
 }
 
-__device__ __forceinline__ uint32_t half2_bits(__half a) {
-  const uint16_t u = __half_as_ushort(a);
-  return static_cast<uint32_t>(u) | (static_cast<uint32_t>(u) << 16);
-}
-
 // One CTA per SM; tile = 128 rows of B (n) x up to 256 rows of A (m), transposed product:
 //   D[n, m] (TMEM, fp32) += Bdq[n, k] (TMEM, f16) . A[m, k] (shared memory, f16)
 // so the expanded B never touches shared memory: the converters store it into TMEM with
@@ -279,24 +274,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       int mb, nb;
       tile_of(tile, tiles_m, tiles_n, mb, nb);
-      const __half* sc_row =
-          p.sc + static_cast<long long>(min(nb * BN + n_local, p.N - 1)) * kgroups;
+      const unsigned short* sc_row = reinterpret_cast<const unsigned short*>(p.sc) +
+                                     static_cast<long long>(min(nb * BN + n_local, p.N - 1)) * kgroups;
       // this group's first stage of the tile, and the scales of the four 16-code groups
       int kb = static_cast<int>(((g - it_base) % WORK_GROUPS + WORK_GROUPS) % WORK_GROUPS);
-      uint32_t s2[4];
+      // raw f16 bits: nothing consumes a prefetched load before its use, so it stays in flight
+      unsigned short sraw[4] = {0, 0, 0, 0};
       if (kb < num_kb) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s2[j] = half2_bits(__ldg(sc_row + (kb * BK + 16 * j) / p.group));
+        for (int j = 0; j < 4; ++j) sraw[j] = __ldg(sc_row + (kb * BK + 16 * j) / p.group);
       }
       for (; kb < num_kb; kb += WORK_GROUPS) {
         const long long it = it_base + kb;
         const int stage = static_cast<int>(it % STAGES);
         const uint32_t phase = static_cast<uint32_t>((it / STAGES) & 1);
-        uint32_t cur[4] = {s2[0], s2[1], s2[2], s2[3]};
+        const unsigned short cur[4] = {sraw[0], sraw[1], sraw[2], sraw[3]};
         if (kb + WORK_GROUPS < num_kb) {  // the next stage's scales, in flight meanwhile
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            s2[j] = half2_bits(__ldg(sc_row + ((kb + WORK_GROUPS) * BK + 16 * j) / p.group));
+            sraw[j] = __ldg(sc_row + ((kb + WORK_GROUPS) * BK + 16 * j) / p.group);
           }
         }
         if (!mbar_wait(&full[stage], phase, abort_flag, p.status, SITE_CONV)) {
@@ -316,10 +312,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           uint32_t v[4];
+          const uint32_t s2 = static_cast<uint32_t>(cur[i / 2]) * 0x10001u;  // (s, s)
           if constexpr (E2M1) {
-            e2m1x8_to_f16(w[i], cur[i / 2], v);
+            e2m1x8_to_f16(w[i], s2, v);
           } else {
-            int4x8_to_f16(w[i], cur[i / 2], v);
+            int4x8_to_f16(w[i], s2, v);
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) o[4 * i + j] = v[j];

@@ -116,12 +116,60 @@ def run(entry: str, problem: Problem, shape: dict[str, Any], data: dict[str, np.
         from torch.profiler import ProfilerActivity, profile
 
         torch.cuda.synchronize()
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        with profile(activities=[ProfilerActivity.CUDA], acc_events=True) as prof:
             got = RUNNERS[entry](tens, shape, outs)
             torch.cuda.synchronize()
-        for ev in prof.events():
-            if ev.device_type.name == "CUDA" and not ev.name.startswith(("Memset", "Memcpy")):
-                launched.append(ev.name)
+        launched.extend(ev.name for ev in prof.events() if ev.device_type.name == "CUDA"
+                        and not ev.name.startswith(("Memset", "Memcpy")))
     if raw:
         return got
     return {name: v.to(torch.float64).cpu().numpy() for name, v in got.items()}
+
+
+def trace_kernels(entry: str, problem: Problem, shape: dict[str, Any],
+                  data: dict[str, np.ndarray], timeout_s: float = 600.0) -> list[str]:
+    """Names of the GPU kernels one launch of ``entry`` puts on the device, traced in a fresh
+    Python process (its first and only CUPTI session), as the reference traces a build in a
+    separate nsys job (src/kta/checks/anticheat.py). A process that has opened many profiler
+    sessions can stop receiving kernel activity records, which would read as "no kernel"."""
+    import json
+    import subprocess
+    import sys
+    import tempfile
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    with tempfile.TemporaryDirectory(prefix="kta_trace_") as d:
+        job = Path(d)
+        np.savez(job / "inputs.npz", **data)
+        (job / "job.json").write_text(json.dumps(
+            {"entry": entry, "problem": problem.model_dump(), "shape": shape},
+            default=lambda v: v.item() if hasattr(v, "item") else str(v)), encoding="utf-8")
+        res = subprocess.run([sys.executable, "-m", "kta_b200.runners", "--trace", str(job)],
+                             cwd=root, capture_output=True, text=True, timeout=timeout_s)
+        if res.returncode != 0:
+            raise RuntimeError(f"kernel trace of {entry} failed:\n{res.stderr[-2000:]}")
+        return list(json.loads((job / "kernels.json").read_text(encoding="utf-8")))
+
+
+def _trace_main(job_dir: str) -> None:
+    import json
+    from pathlib import Path
+
+    job = Path(job_dir)
+    spec = json.loads((job / "job.json").read_text(encoding="utf-8"))
+    with np.load(job / "inputs.npz") as z:
+        data = {k: z[k] for k in z.files}
+    names: list[str] = []
+    run(spec["entry"], Problem.model_validate(spec["problem"]), spec["shape"], data,
+        nan_fill=True, raw=True, launched=names)
+    (job / "kernels.json").write_text(json.dumps(names), encoding="utf-8")
+
+
+if __name__ == "__main__":
+    import sys
+
+    if len(sys.argv) == 3 and sys.argv[1] == "--trace":
+        _trace_main(sys.argv[2])
+    else:
+        raise SystemExit("usage: python -m kta_b200.runners --trace <job dir>")
