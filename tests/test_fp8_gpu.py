@@ -42,8 +42,10 @@ def _check(y, ref):
     assert np.linalg.norm(y - ref) <= 2e-2 * np.linalg.norm(ref)
 
 
+# 18944 x 256: 148 tiles of 128 x 256, exactly one per SM of a B200.
 @pytest.mark.parametrize("m,n,k", [(128, 256, 128), (256, 512, 1024), (300, 520, 208),
-                                   (1, 256, 128), (130, 136, 4096), (512, 1024, 7168)])
+                                   (1, 256, 128), (130, 136, 4096), (512, 1024, 7168),
+                                   (18944, 256, 256)])
 def test_fp8_blockscaled(cuda_device, m, n, k):
     ac, sa, bc, sb = _make(m, n, k)
     y = _run(cuda_device, ac, sa, bc, sb)
