@@ -12,12 +12,13 @@
 //
 //   * warp 0: TMA producer; per 64-deep K stage the A tile (up to 256 rows x 64 f16, 128-byte
 //     swizzle; the MMA's B operand) and the packed B tile (128 rows x 32 bytes), 6 stages;
-//   * warps 6-13: converters; two per TMEM lane quarter, each thread expands 32 codes of one
-//     B row and stores them with tcgen05.st into the stage's TMEM slot (one arrival per warp);
 //   * warp 1: TMEM owner and single-thread MMA issuer, M = 128 (B rows) x N = the m tile
 //     (256, or M rounded up to 16 when one tile covers M), 4 MMAs of K = 16 per stage;
-//   * warps 2-5: epilogue; thread = one B row n: TMEM columns are m, neighbouring lanes swap
-//     halves so each stores an (n, n + 1) pair of C[m, :];
+//   * warps 2-17: workers in four stage groups (one warp per TMEM lane quarter per group):
+//     the stages are dealt round-robin to the groups, a thread expands all 64 codes of its B
+//     row with scales fetched one group-turn ahead and stores them with tcgen05.st into the
+//     stage's TMEM slot; at the end of a tile all sixteen drain the accumulator (64 columns
+//     each; neighbouring lanes swap halves so each stores an (n, n + 1) pair of C[m, :]);
 //   * persistent grid, grouped raster of tiles; every mbarrier wait is bounded.
 //
 // Shared memory carries only the TMA writes and the tensor core's reads of A (68 KB per stage
@@ -188,6 +189,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_launch_dependents();
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
   const int mt = p.m_tile;
   const int tiles_m = (p.M + mt - 1) / mt;
   const int tiles_n = (p.N + BN - 1) / BN;
@@ -424,8 +427,8 @@ int launch(const void* A, const void* Bq, const void* Sc, void* C, int64_t M64, 
   if (s != KTA_OK) return s;
   const int tiles = ((M + mt - 1) / mt) * ((N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, current_sm_count()));
-  kernel<<<grid, NUM_THREADS, Layout::ALLOC, static_cast<cudaStream_t>(stream_v)>>>(ta, tq, prm);
-  return launch_status();
+  return launch_ex(kernel, dim3(grid), dim3(NUM_THREADS), Layout::ALLOC,
+                   static_cast<cudaStream_t>(stream_v), 1, ta, tq, prm);
 }
 
 }  // namespace dq
