@@ -228,6 +228,15 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
                : "memory");
 }
 
+// Programmatic dependent launch (kernels launched by launch_ex): let the next grid of the
+// stream be scheduled, and hold this thread until the previous grid has completed and its
+// memory writes are visible. Every thread of a kernel calls both after its set-up and before
+// its first global-memory access; without the launch attribute the wait returns at once.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }

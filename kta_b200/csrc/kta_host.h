@@ -42,4 +42,37 @@ int set_kernel_smem(const void* kernel, int bytes);
 // Status of the last kta_so_* call on this host thread (kta_last_error).
 void set_last_error(int s);
 
+// Launches `kernel` with programmatic stream serialisation: the next kernel in the stream (or
+// graph) may be scheduled and run its set-up while this one finishes; its griddepcontrol.wait
+// holds every memory access until this grid has completed and its writes are visible.
+// cluster_x > 1 launches clusters of that many CTAs.
+template <typename... KArgs, typename... Args>
+int launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+              unsigned cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  if (cudaLaunchKernelEx(&cfg, kernel, args...) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return KTA_ERR_LAUNCH;
+  }
+  return launch_status();
+}
+
 }  // namespace kta
