@@ -334,6 +334,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_launch_dependents();
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
   const int num_units = p.batch * p.heads * p.pairs;
   const int rounds = (num_units + gridDim.x - 1) / gridDim.x;
 
@@ -636,8 +638,8 @@ int launch(const void* Q, const void* K, const void* V, void* O, void* LSE, int6
   if (s != KTA_OK) return s;
   const long long units = B * H * static_cast<long long>(prm.pairs);
   const int grid = static_cast<int>(std::max(1LL, std::min<long long>(current_sm_count(), units)));
-  attn_fwd_kernel<<<grid, NUM_THREADS, Layout::ALLOC, stream>>>(tq, tk, tv, prm);
-  return launch_status();
+  return launch_ex(attn_fwd_kernel, dim3(grid), dim3(NUM_THREADS), Layout::ALLOC, stream, 1, tq,
+                   tk, tv, prm);
 }
 
 }  // namespace attn

@@ -190,6 +190,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int B = p.batch;
   const int G = p.group;
 
+  pdl_launch_dependents();
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
   // ---- lengths, validation and the tile prefix (every CTA computes the same table) ----
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     const int len = p.seqlens[b];
@@ -625,8 +627,8 @@ int launch(const void* Q, const void* Kc, const void* Vc, const void* seqlens,
   auto go = [&](auto kernel) -> int {
     int st = set_kernel_smem(reinterpret_cast<const void*>(kernel), 232448);
     if (st != KTA_OK) return st;
-    kernel<<<grid, NUM_THREADS, smem_bytes, stream>>>(tk, tv, tq, prm);
-    return KTA_OK;
+    return launch_ex(kernel, dim3(grid), dim3(NUM_THREADS), smem_bytes, stream, 1, tk, tv, tq,
+                     prm);
   };
   if (group <= 8) {
     s = three ? go(decode_kernel<3, 1>) : go(decode_kernel<2, 1>);

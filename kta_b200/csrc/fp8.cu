@@ -115,6 +115,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_launch_dependents();
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
   const int tiles_m = (p.M + BM - 1) / BM;
   const int tiles_n = (p.N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
@@ -306,8 +308,8 @@ int launch(const void* A, const void* sa, const void* B, const void* sb, void* C
   if (s != KTA_OK) return s;
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, current_sm_count()));
-  fp8_gemm_kernel<<<grid, NUM_THREADS, Layout::ALLOC, stream>>>(ta, tb, prm);
-  return launch_status();
+  return launch_ex(fp8_gemm_kernel, dim3(grid), dim3(NUM_THREADS), Layout::ALLOC, stream, 1, ta,
+                   tb, prm);
 }
 
 }  // namespace fp8

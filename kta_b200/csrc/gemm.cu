@@ -123,6 +123,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_launch_dependents();
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
 
   const int tiles_m = (M + BM - 1) / BM;
   const int tiles_n = (N + BN - 1) / BN;
@@ -359,6 +361,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   pair_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_launch_dependents();
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
 
   const int tiles_m = (M + P_BM - 1) / P_BM;
   const int tiles_n = (N + P_BN - 1) / P_BN;
@@ -599,6 +603,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   cluster_sync_all();  // every CTA of the cluster runs before any DSMEM access
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_launch_dependents();
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
 
   if (warp == 0) {
     if (lane == 0) {
@@ -782,9 +788,8 @@ int launch_main(const void* A, const void* B, void* C, int M, int N, int K, int6
   const int sms = current_sm_count();
   const int grid = std::max(1, std::min(tiles, sms));
   const int rows_per_group = groups > 0 ? M / groups : 0;
-  kernel<<<grid, NUM_THREADS, L::ALLOC, stream>>>(ta, tb, tc, M, N, K, rows_per_group,
-                                                   device_status_ptr());
-  return launch_status();
+  return launch_ex(kernel, dim3(grid), dim3(NUM_THREADS), L::ALLOC, stream, 1, ta, tb, tc, M, N,
+                   K, rows_per_group, device_status_ptr());
 }
 
 template <int MP, bool BF16>
@@ -821,26 +826,10 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
     cs *= 2;
   }
 
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles * cs), 1, 1);
-  cfg.blockDim = dim3(SK_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = L::ALLOC;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(cs);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   void* Cp = C;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, Cp, M, N, K, ldc, cs,
-                                     device_status_ptr());
-  if (e != cudaSuccess) {
-    (void)cudaGetLastError();
-    return KTA_ERR_LAUNCH;
-  }
-  return launch_status();
+  return launch_ex(kernel, dim3(static_cast<unsigned>(tiles * cs)), dim3(SK_THREADS), L::ALLOC,
+                   stream, static_cast<unsigned>(cs), ta, tb, Cp, M, N, K, ldc, cs,
+                   device_status_ptr());
 }
 
 template <bool BF16>
@@ -876,24 +865,8 @@ int launch_pair(const void* A, const void* B, void* C, int M, int N, int K, int6
   if (s != KTA_OK) return s;
   const int tiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
   const int pairs = std::max(1, std::min(tiles, current_sm_count() / 2));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = L::ALLOC;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, M, N, K, device_status_ptr());
-  if (e != cudaSuccess) {
-    (void)cudaGetLastError();
-    return KTA_ERR_LAUNCH;
-  }
-  return launch_status();
+  return launch_ex(kernel, dim3(static_cast<unsigned>(2 * pairs)), dim3(NUM_THREADS), L::ALLOC,
+                   stream, 2, ta, tb, tc, M, N, K, device_status_ptr());
 }
 
 // Estimated relative time of a tile width: waves x columns, discounted by how close the

@@ -126,6 +126,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmB);
   }
   __syncthreads();
+  pdl_launch_dependents();
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
 
   if (warp == 0) {
     if (lane == 0) {
@@ -260,8 +262,8 @@ int launch_nt(const void* A, const void* B, void* C, int M, int N, int K, int64_
   if (s != KTA_OK) return s;
   const int tiles8 = (N + 7) / 8;
   const int grid = (tiles8 + NT - 1) / NT;
-  kernel<<<grid, THREADS, L::ALLOC, stream>>>(ta, tb, C, M, N, K, ldc, device_status_ptr());
-  return launch_status();
+  return launch_ex(kernel, dim3(grid), dim3(THREADS), L::ALLOC, stream, 1, ta, tb, C, M, N, K,
+                   ldc, device_status_ptr());
 }
 
 }  // namespace m16

@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(THREADS)
     rowop_kernel(const T* __restrict__ X, const T* __restrict__ W, T* __restrict__ Y, int M,
                  int N, float eps) {
   __shared__ float red[THREADS / 32];
+  pdl_launch_dependents();
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
   constexpr int VEC = 8;                 // 16-byte vectors of 16-bit elements
   constexpr int NV = EPT / VEC;          // vectors per thread
   const int g = threadIdx.x % G;
@@ -143,9 +145,9 @@ int launch_cfg(const void* X, const void* W, void* Y, int M, int N, float eps,
   const long long rows_per_cta = THREADS / G;
   const long long grid = (M + rows_per_cta - 1) / rows_per_cta;
   if (grid > 0x7fffffffLL) return KTA_ERR_UNSUPPORTED;
-  rowop_kernel<G, EPT, T, OP><<<static_cast<unsigned>(grid), THREADS, 0, stream>>>(
-      static_cast<const T*>(X), static_cast<const T*>(W), static_cast<T*>(Y), M, N, eps);
-  return launch_status();
+  return launch_ex(rowop_kernel<G, EPT, T, OP>, dim3(static_cast<unsigned>(grid)), dim3(THREADS),
+                   0, stream, 1, static_cast<const T*>(X), static_cast<const T*>(W),
+                   static_cast<T*>(Y), M, N, eps);
 }
 
 // Threads per row: the smallest power of two >= 32 that keeps a thread at <= 32 elements
