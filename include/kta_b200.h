@@ -58,6 +58,13 @@ int kta_device_status(uint32_t* words, int clear);
 /* Number of SMs of the current device (the persistent grids' size). */
 int kta_sm_count(void);
 
+/* Self-test of the device watchdog every kernel's waits go through (no counterpart in the
+ * reference, whose kernels have no device-side waits): one thread waits for a barrier phase
+ * that nothing completes, gives up after timeout_ns (1 us .. 10 s) of %globaltimer, records
+ * KTA_ERR_DEVICE_TIMEOUT with site 0x7F01 in the device status block and returns, leaving the
+ * context usable. Asynchronous on `stream`; read the outcome with kta_device_status. */
+int kta_watchdog_selftest(uint64_t timeout_ns, void* stream);
+
 /* --- GEMM: C[M,N] = A[M,K] . B[N,K]^T, fp32 accumulate --------------------------------
  * Replaces the TileLang `hgemm` case (perfmodel/testset/gen.py:255-303) and the seed GEMM
  * family (knowledge/seed/families/gemm_fp16_tilelang/gen.py:32-112), launched like

@@ -19,7 +19,8 @@ namespace kta {
 
 // ---------------------------------------------------------------------------------------
 // Watchdog: every wait on an mbarrier is bounded. On expiry the waiting thread records
-// where it gave up in the device status block (kta_status.h) and the kernel unwinds.
+// where it gave up in the device status block (read by kta_device_status) and the kernel
+// unwinds.
 // ---------------------------------------------------------------------------------------
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s of %globaltimer
 
@@ -104,11 +105,13 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_
 }
 
 // Waits for the phase with parity `parity` of `bar` to complete. Returns false if the wait
-// ran past kWaitTimeoutNs or if another role of the CTA already aborted (`*abort` != 0);
-// in the first case it raises `*abort` and records `site` in the status block.
+// ran past `timeout_ns` (kWaitTimeoutNs in every kernel) or if another role of the CTA
+// already aborted (`*abort` != 0); in the first case it raises `*abort` and records `site`
+// in the status block.
 template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          unsigned int* status, unsigned int site) {
+                                          unsigned int* status, unsigned int site,
+                                          uint64_t timeout_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_u32(bar);
   if ((CLUSTER ? mbar_try_wait_cluster(a, parity) : mbar_try_wait(a, parity))) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -118,7 +121,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       if ((CLUSTER ? mbar_try_wait_cluster(a, parity) : mbar_try_wait(a, parity))) return true;
     }
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
       *abort = 1;
       record_status(status, KTA_ERR_DEVICE_TIMEOUT, site);
       return false;

@@ -6,6 +6,7 @@
 
 #include <cudaTypedefs.h>
 
+#include "kta_common.cuh"
 #include "kta_host.h"
 
 namespace {
@@ -138,9 +139,44 @@ int set_kernel_smem(const void* kernel, int bytes) {
 
 }  // namespace kta
 
+namespace {
+
+// Site recorded by the watchdog self-test.
+constexpr unsigned int kSelftestSite = 0x7F01;
+
+// One thread waits, through the kernels' own bounded wait, for a phase of a barrier that no
+// thread ever completes: the wait expires after `timeout_ns`, records KTA_ERR_DEVICE_TIMEOUT
+// and the site, and the kernel returns. Nothing faults and nothing is left waiting.
+__global__ void watchdog_selftest_kernel(unsigned int* status, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    kta::mbar_init(&bar, 1);
+    abort_flag = 0;
+    kta::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    (void)kta::mbar_wait(&bar, 0u, &abort_flag, status, kSelftestSite, timeout_ns);
+  }
+}
+
+}  // namespace
+
 extern "C" {
 
 int kta_abi_version(void) { return KTA_ABI_VERSION; }
+
+int kta_watchdog_selftest(uint64_t timeout_ns, void* stream) {
+  if (timeout_ns < 1000ull || timeout_ns > 10000000000ull) return KTA_ERR_INVALID_ARG;
+  int s = kta::require_sm100();
+  if (s != KTA_OK) return s;
+  unsigned int* status = kta::device_status_ptr();
+  if (status == nullptr) return KTA_ERR_NO_DEVICE;
+  watchdog_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      status, static_cast<unsigned long long>(timeout_ns));
+  return kta::launch_status();
+}
 
 const char* kta_status_string(int status) {
   switch (status) {

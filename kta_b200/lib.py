@@ -40,6 +40,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kta_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "kta_device_status": (ctypes.c_int, [ctypes.POINTER(_u32), ctypes.c_int]),
     "kta_sm_count": (ctypes.c_int, []),
+    "kta_watchdog_selftest": (ctypes.c_int, [_u64, _ptr]),
     "kta_last_error": (ctypes.c_int, []),
     "kta_gemm_bf16": (ctypes.c_int, [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _ptr]),
     "kta_gemm_f16": (ctypes.c_int, [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _ptr]),

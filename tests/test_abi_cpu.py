@@ -156,3 +156,9 @@ def test_so_shim_reports_through_last_error():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(lib.KtaLibraryError):
         lib.load(tmp_path / "nope.so")
+
+
+def test_watchdog_selftest_argument_checks():
+    L = lib.load()
+    assert L.kta_watchdog_selftest(0, None) == 1            # below 1 us
+    assert L.kta_watchdog_selftest(20_000_000_000, None) == 1  # above 10 s
