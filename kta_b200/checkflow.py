@@ -50,8 +50,8 @@ SKIPPED = {
 
 # ---- hidden shapes (src/kta/checks/hidden.py) ----------------------------------------------
 def private_seed(private_dir: str | Path | None = None) -> str:
-    """The checker's private seed: drawn once from the OS, kept mode 600 outside any
-    workspace (hidden.py:24-31)."""
+    """The private seed of the hidden-shape check: drawn once from the OS, kept mode 600
+    outside any workspace (hidden.py:24-31)."""
     d = Path(private_dir or os.environ.get("KTA_B200_CHECKER_DIR",
                                            Path.home() / ".kta_b200" / "checker"))
     path = d / "hidden_seed"

@@ -2,7 +2,7 @@
 
 TEST INFRASTRUCTURE ONLY. Only tests/, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU
 baseline leg (``--impl reference`` and the ``cpu_baseline`` field) import this package, and
-only as the checker or as the timed CPU reference implementation; the product path
+only to check results or as the timed CPU reference implementation; the product path
 (kta_b200) never imports, calls or links anything here.
 
 Contents, each citing the reference code it restates (paths within kernel-template-agent):
