@@ -12,11 +12,12 @@ on the data path; the total work is fixed as N grows ("scaling": "strong").
 
 A step is one launch of the hot-path kernel over one rotating input set already resident in
 HBM (at least 4 sets, and as many as make the sets together twice the 126 MB L2, so no flush
-is needed between steps). Rank 0 prints one JSON line: the driver's keys plus `roofline` (the dominant kernel's
-achieved rate from CUDA events against MEASURED_PEAKS.json), `sol` (the case's L1
-speed-of-light bound, as KTA reports pct_of_bound), `e2e` (the same metric through the
-public API with pinned host inputs copied in and the result copied out every step),
-`cpu_baseline` (the reference's CPU torch path timed on a bounded sample) and `clocks`.
+is needed between steps). Rank 0 prints one JSON line: the driver's keys plus `roofline` (the
+dominant kernel's achieved rate from CUDA events against MEASURED_PEAKS.json), `sol` (the
+case's L1 speed-of-light bound, as KTA reports pct_of_bound), `e2e` (the same metric through
+the public API with pinned host inputs copied in and the result copied out every step, two
+steps in flight on two streams), `cpu_baseline` (the reference's CPU torch path timed on a
+bounded sample) and `clocks`.
 
 `--impl reference` times the reference's own CPU implementation of the path instead: the
 case statement run by torch on the host cores in the inputs' dtype, i.e. the "library"
@@ -55,6 +56,8 @@ def sets_for(bytes_per_set: float) -> int:
     if "KTA_BENCH_SETS" in os.environ:
         return NSETS
     return max(NSETS, int(-(-2 * L2_BYTES // max(int(bytes_per_set), 1))))
+
+
 CPU_BUDGET_S = 12.0  # CPU baseline sample: about this much host compute
 
 
@@ -406,6 +409,12 @@ class DecodeWorkload:
                          device="cpu").pin_memory()
         self.hv = _randn((self.tokens, self.hkv, self.d), torch.bfloat16, g,
                          device="cpu").pin_memory()
+        # its own split-KV workspace: two end-to-end pipelines run at once and never share one
+        from kta_b200 import ops
+
+        self.ws = torch.zeros(ops.decode_workspace_bytes(self.b, self.hq, self.hkv, self.d,
+                                                         self.max_seqlen),
+                              dtype=torch.uint8, device=device)
         self.hsl = torch.tensor(self.lengths, dtype=torch.int32).pin_memory()
         self.hoff = torch.tensor(self._offsets(), dtype=torch.int64).pin_memory()
         self.ho = torch.empty((self.b, self.hq, self.d), dtype=torch.bfloat16).pin_memory()
@@ -1086,21 +1095,38 @@ def time_device_graph(wl, steps: int, warmup: int, dist: Dist) -> dict:
             "graph": True}
 
 
-def time_e2e(wl, steps: int, dist: Dist) -> dict:
-    stream = torch.cuda.current_stream()
-    for _ in range(2):
-        wl.e2e_step()
+def time_e2e(wl, steps: int, dist: Dist, device: torch.device) -> dict:
+    """Steps through the public API with pinned host buffers, each step copying its inputs
+    in and its result out. Consecutive steps alternate between two pipelines (own host and
+    device buffers, own stream), as a serving loop overlaps them: one step's read-back runs
+    beside the next step's upload on the full-duplex link."""
+    import copy
+
+    main = torch.cuda.current_stream()
+    pipes = [wl, copy.copy(wl)]
+    pipes[1].setup_e2e(device)  # new buffers on the copy; the workload keeps its own
+    streams = [torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)]
+
+    def run(n: int) -> None:
+        for st in streams:
+            st.wait_stream(main)
+        for s in range(n):
+            with torch.cuda.stream(streams[s % 2]):
+                pipes[s % 2].e2e_step()
+        for st in streams:
+            main.wait_stream(st)
+
+    run(2)
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        wl.e2e_step()
-    e1.record(stream)
+    e0.record(main)
+    run(steps)
+    e1.record(main)
     torch.cuda.synchronize()
     dist.barrier()
-    return {"total_ms": e0.elapsed_time(e1)}
+    return {"total_ms": e0.elapsed_time(e1), "pipelines": 2}
 
 
 def calibrate_cpu(wl, budget_s: float):
@@ -1209,7 +1235,7 @@ def run_kta(args, dist: Dist) -> dict | None:
     # end to end through the public API with host buffers
     wl.setup_e2e(device)
     e2e_steps = max(3, min(args.steps, 20))
-    e2e = time_e2e(wl, e2e_steps, dist)
+    e2e = time_e2e(wl, e2e_steps, dist, device)
     e2e_ms = dist.max(e2e["total_ms"])
     e2e_value = world_work * e2e_steps / (e2e_ms / 1e3) / scale
     result = None
@@ -1239,7 +1265,10 @@ def run_kta(args, dist: Dist) -> dict | None:
                     "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
                     "steps": e2e_steps,
                     "path": "pinned host -> device copies, libkta_b200 C-ABI launch, "
-                            "device -> pinned host copy, every step"},
+                            "device -> pinned host copy, every step; consecutive steps on "
+                            "two streams with their own buffers (one step's read-back "
+                            "beside the next one's upload)",
+                    "pipelines": e2e.get("pipelines", 1)},
             "cpu_baseline": cpu,
             "clocks": ck,
             "gpu_launches": args.steps,
