@@ -131,14 +131,24 @@ def shard(n: int, parts: int, i: int, align: int = 1) -> tuple[int, int]:
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------------------
 class Clocks:
+    """SM clock, power and clock-event reasons of this rank's GPU, polled every 5 ms through
+    NVML (read-only queries) on a background thread, so that even a timed region of a few
+    milliseconds holds samples; nvidia-smi at its 100 ms floor is the fallback when NVML
+    cannot be opened. Nothing here changes a GPU setting."""
+
     FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
+    PERIOD_S = 0.005
 
     def __init__(self) -> None:
         self.samples: list[tuple[float, dict[str, str]]] = []
         self.proc: subprocess.Popen | None = None
         self.thread: threading.Thread | None = None
+        self.stop_flag = threading.Event()
+        self.source = "none"
         self.bus: tuple[int, int, int] | None = None
         try:
             p = torch.cuda.get_device_properties(torch.cuda.current_device())
@@ -155,7 +165,47 @@ class Clocks:
         except (KeyError, ValueError):
             return False
 
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        if self.bus is None:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(0)
+        dom, bus, dev = self.bus
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dev:02x}.0")
+
     def start(self) -> None:
+        try:
+            nv, h = self._nvml_handle()
+            max_sm = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            bus_id = nv.nvmlDeviceGetPciInfo(h).busId
+            bus_id = bus_id.decode() if isinstance(bus_id, bytes) else str(bus_id)
+        except Exception:
+            self._start_smi()
+            return
+        self.source = "nvml (5 ms)"
+
+        def poll() -> None:
+            while not self.stop_flag.is_set():
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    rs = int(reasons_fn(h))
+                except Exception:
+                    break
+                s = {"pci.bus_id": bus_id, "clocks.sm": str(sm), "clocks.max.sm": str(max_sm),
+                     "power.draw": f"{pw:.2f}"}
+                for k, bit in self.REASON_BITS.items():
+                    s[f"clocks_event_reasons.{k}"] = "Active" if rs & bit else "Not Active"
+                self.samples.append((time.time(), s))
+                time.sleep(self.PERIOD_S)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+
+    def _start_smi(self) -> None:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -163,6 +213,7 @@ class Clocks:
         except OSError:
             self.proc = None
             return
+        self.source = "nvidia-smi (100 ms)"
         keys = self.FIELDS.split(",")
 
         def reader() -> None:
@@ -176,19 +227,24 @@ class Clocks:
         self.thread.start()
 
     def stop(self) -> None:
+        self.stop_flag.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
 
     def summary(self, t0: float, t1: float) -> dict:
         mine = [s for t, s in self.samples if self._mine(s)]
-        inside = [s for t, s in self.samples if t0 - 0.15 <= t <= t1 + 0.15 and self._mine(s)]
-        use = inside or mine[-3:]
+        inside = [s for t, s in self.samples if t0 <= t <= t1 and self._mine(s)]
+        use = inside or [s for t, s in self.samples if t0 - 0.15 <= t <= t1 + 0.15
+                         and self._mine(s)] or mine[-3:]
         if not use:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "source": self.source}
 
         def num(s: dict, k: str) -> float | None:
             try:
@@ -200,17 +256,20 @@ class Clocks:
         reasons = set()
         for s in use:
             for k in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
-                      "sw_power_cap"):
+                      "sw_power_cap", "hw_power_brake_slowdown"):
                 if s.get(f"clocks_event_reasons.{k}", "").strip().lower() == "active":
                     reasons.add(k)
         power = [v for v in (num(s, "power.draw") for s in use) if v is not None]
         return {
             "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_mhz_min": min(sm) if sm else None,
+            "sm_mhz_max": max(sm) if sm else None,
             "sm_max_mhz": num(use[0], "clocks.max.sm"),
             "reasons": sorted(reasons),
             "power_w_max": max(power) if power else None,
             "samples": len(use),
             "samples_in_timed_region": len(inside),
+            "source": self.source,
         }
 
 
@@ -270,7 +329,7 @@ class GemmWorkload:
         }
 
     def setup(self, device: torch.device) -> None:
-        g = torch.Generator(device=device).manual_seed(1234)
+        g = torch.Generator(device=device).manual_seed(0)
         s = 1.0 / math.sqrt(self.k)
         self.a = [_randn((self.m, self.k), self.dtype, g, s) for _ in range(self.nsets)]
         self.b = [_randn((self.n, self.k), self.dtype, g, s) for _ in range(self.nsets)]
@@ -283,16 +342,17 @@ class GemmWorkload:
         j = i % self.nsets
         ops.gemm(self.a[j], self.b[j], out=self.c[j])
 
+    def gather_tensors(self) -> list[torch.Tensor]:
+        """This rank's output block for the optional all-gather: C[:, n0:n0+n] of set 0."""
+        return [self.c[0]]
+
     # ---- end to end: pinned host inputs in, result out, every step ----
-    def setup_e2e(self, device: torch.device) -> None:
-        g = torch.Generator().manual_seed(99)
+    def setup_e2e(self, device: torch.device, seed: int = 99) -> None:
+        g = torch.Generator().manual_seed(seed)
         s = 1.0 / math.sqrt(self.k)
         self.ha = _randn((self.m, self.k), self.dtype, g, s, device="cpu").pin_memory()
         self.hb = _randn((self.n, self.k), self.dtype, g, s, device="cpu").pin_memory()
         self.hc = torch.empty((self.m, self.n), dtype=self.dtype).pin_memory()
-        self.da = torch.empty_like(self.ha, device=device)
-        self.db = torch.empty_like(self.hb, device=device)
-        self.dc = torch.empty_like(self.hc, device=device)
         self.h2d_bytes = self.ha.numel() * self.esize + self.hb.numel() * self.esize
         self.d2h_bytes = self.hc.numel() * self.esize
 
@@ -300,8 +360,10 @@ class GemmWorkload:
         from kta_b200 import ops
 
         # the public host-buffer entry: B, then A in row blocks copied in, each block's GEMM
-        # as soon as it landed, C blocks copied out behind it (copies overlap compute)
-        ops.gemm_host(self.ha, self.hb, out=self.hc)
+        # as soon as it landed, C blocks copied out behind it (copies overlap compute); device
+        # buffers of its own per caller stream; returns once queued, C valid on the host when
+        # the caller's stream reaches this point
+        ops.gemm_host(self.ha, self.hb, out=self.hc, wait=False)
 
     # ---- the reference's CPU torch path on a bounded sample ----
     def cpu_sample(self, rows: int):
@@ -385,7 +447,7 @@ class DecodeWorkload:
     def setup(self, device: torch.device) -> None:
         from kta_b200 import ops
 
-        g = torch.Generator(device=device).manual_seed(4321)
+        g = torch.Generator(device=device).manual_seed(0)
         self.q = [_randn((self.b, self.hq, self.d), torch.bfloat16, g) for _ in range(NSETS)]
         self.kc = [_randn((self.tokens, self.hkv, self.d), torch.bfloat16, g) for _ in range(NSETS)]
         self.vc = [_randn((self.tokens, self.hkv, self.d), torch.bfloat16, g) for _ in range(NSETS)]
@@ -402,8 +464,8 @@ class DecodeWorkload:
         ops.decode_gqa(self.q[j], self.kc[j], self.vc[j], self.sl, self.off, self.max_seqlen,
                        out=self.o[j], workspace=self.ws)
 
-    def setup_e2e(self, device: torch.device) -> None:
-        g = torch.Generator().manual_seed(99)
+    def setup_e2e(self, device: torch.device, seed: int = 99) -> None:
+        g = torch.Generator().manual_seed(seed)
         self.hq_ = _randn((self.b, self.hq, self.d), torch.bfloat16, g, device="cpu").pin_memory()
         self.hk = _randn((self.tokens, self.hkv, self.d), torch.bfloat16, g,
                          device="cpu").pin_memory()
@@ -483,7 +545,9 @@ class AttnWorkload:
         self.b_total, self.h, self.s, self.d = b, h, s, d
         pairs = b * h
         lo, hi = shard(pairs, dist.world, dist.rank)
-        # whole batches when the split allows it, otherwise heads of one batch entry
+        # (batch, head) pairs lo .. hi - 1 in batch-major order; whole batches when the split
+        # allows it (every N of 1, 2, 4, 8), otherwise heads of one batch entry
+        self.pair_lo, self.pair_hi = lo, hi
         self.pairs = hi - lo
         if self.pairs % h == 0:
             self.b, self.hh = self.pairs // h, h
@@ -518,7 +582,7 @@ class AttnWorkload:
                 "inputs": "N(0,1) bf16 from a seeded torch generator"}
 
     def setup(self, device: torch.device) -> None:
-        g = torch.Generator(device=device).manual_seed(77)
+        g = torch.Generator(device=device).manual_seed(0)
         shp = (self.b, self.s, self.hh, self.d)
         self.qkv = [[_randn(shp, torch.bfloat16, g) for _ in range(3)] for _ in range(NSETS)]
         self.o = [torch.empty(shp, dtype=torch.bfloat16, device=device) for _ in range(NSETS)]
@@ -532,8 +596,12 @@ class AttnWorkload:
         q, k, v = self.qkv[j]
         ops.attn_fwd_causal(q, k, v, out=self.o[j], lse=self.lse[j])
 
-    def setup_e2e(self, device: torch.device) -> None:
-        g = torch.Generator().manual_seed(99)
+    def gather_tensors(self) -> list[torch.Tensor]:
+        """This rank's O and LSE of set 0 (whole batch entries) for the optional all-gather."""
+        return [self.o[0], self.lse[0]]
+
+    def setup_e2e(self, device: torch.device, seed: int = 99) -> None:
+        g = torch.Generator().manual_seed(seed)
         shp = (self.b, self.s, self.hh, self.d)
         self.hqkv = [_randn(shp, torch.bfloat16, g, device="cpu").pin_memory() for _ in range(3)]
         self.ho = torch.empty(shp, dtype=torch.bfloat16).pin_memory()
@@ -624,7 +692,7 @@ class Fp8Workload:
         return q, scale.contiguous()
 
     def setup(self, device: torch.device) -> None:
-        g = torch.Generator(device=device).manual_seed(55)
+        g = torch.Generator(device=device).manual_seed(0)
         self.sets = []
         for _ in range(NSETS):
             a = torch.randn(self.m, self.k, generator=g, device=device)
@@ -644,8 +712,8 @@ class Fp8Workload:
         j = i % NSETS
         ops.gemm_fp8_blockscaled(*self.sets[j], out=self.c[j])
 
-    def setup_e2e(self, device: torch.device) -> None:
-        qa, sa, qb, sb = self.sets[0]
+    def setup_e2e(self, device: torch.device, seed: int = 99) -> None:
+        qa, sa, qb, sb = self.sets[seed % len(self.sets)]  # each pipeline its own input set
         self.h = [t.cpu().pin_memory() for t in (qa.view(torch.uint8), sa, qb.view(torch.uint8), sb)]
         self.dv = [torch.empty_like(t, device=device) for t in self.h]
         self.hc = torch.empty((self.m, self.n), dtype=torch.bfloat16).pin_memory()
@@ -729,7 +797,7 @@ class MoeWorkload:
                 "inputs": "N(0,1)/sqrt(K) f16 from a seeded torch generator"}
 
     def setup(self, device: torch.device) -> None:
-        g = torch.Generator(device=device).manual_seed(2468)
+        g = torch.Generator(device=device).manual_seed(0)
         s = 1.0 / math.sqrt(self.k)
         self.a = [_randn((self.t, self.k), torch.float16, g, s) for _ in range(self.nsets)]
         self.w = [_randn((self.e, self.k, self.n), torch.float16, g, s)
@@ -743,8 +811,8 @@ class MoeWorkload:
         j = i % self.nsets
         ops.moe_gemm(self.a[j], self.w[j], out=self.c[j])
 
-    def setup_e2e(self, device: torch.device) -> None:
-        g = torch.Generator().manual_seed(99)
+    def setup_e2e(self, device: torch.device, seed: int = 99) -> None:
+        g = torch.Generator().manual_seed(seed)
         s = 1.0 / math.sqrt(self.k)
         self.ha = _randn((self.t, self.k), torch.float16, g, s, device="cpu").pin_memory()
         self.hw = _randn((self.e, self.k, self.n), torch.float16, g, s, device="cpu").pin_memory()
@@ -836,7 +904,7 @@ class Dq4Workload:
         return torch.from_numpy(bq), torch.from_numpy(sc)
 
     def setup(self, device: torch.device) -> None:
-        g = torch.Generator(device=device).manual_seed(1357)
+        g = torch.Generator(device=device).manual_seed(0)
         s = 1.0 / math.sqrt(self.k)
         hbq, hsc = self._quantised(self.n, 11)
         self.sets = [(_randn((self.m, self.k), torch.float16, g, s), hbq.to(device),
@@ -850,8 +918,8 @@ class Dq4Workload:
         j = i % self.nsets
         ops.gemm_4bit(*self.sets[j], self.fmt, self.group, out=self.c[j])
 
-    def setup_e2e(self, device: torch.device) -> None:
-        g = torch.Generator().manual_seed(99)
+    def setup_e2e(self, device: torch.device, seed: int = 99) -> None:
+        g = torch.Generator().manual_seed(seed)
         self.ha = _randn((self.m, self.k), torch.float16, g, 1.0 / math.sqrt(self.k),
                          device="cpu").pin_memory()
         bq, sc = self._quantised(self.n, 12)
@@ -935,7 +1003,7 @@ class RowOpWorkload:
                 "inputs": "N(0,1) f16 from a seeded torch generator"}
 
     def setup(self, device: torch.device) -> None:
-        g = torch.Generator(device=device).manual_seed(4321)
+        g = torch.Generator(device=device).manual_seed(0)
         self.x = [_randn((self.m, self.n), torch.float16, g) for _ in range(NSETS)]
         self.y = [torch.empty((self.m, self.n), dtype=torch.float16, device=device)
                   for _ in range(NSETS)]
@@ -953,8 +1021,8 @@ class RowOpWorkload:
         j = i % NSETS
         self._run(self.x[j], self.y[j])
 
-    def setup_e2e(self, device: torch.device) -> None:
-        g = torch.Generator().manual_seed(99)
+    def setup_e2e(self, device: torch.device, seed: int = 99) -> None:
+        g = torch.Generator().manual_seed(seed)
         self.hx = _randn((self.m, self.n), torch.float16, g, device="cpu").pin_memory()
         self.hy = torch.empty((self.m, self.n), dtype=torch.float16).pin_memory()
         self.dx = torch.empty_like(self.hx, device=device)
@@ -1104,7 +1172,8 @@ def time_e2e(wl, steps: int, dist: Dist, device: torch.device) -> dict:
 
     main = torch.cuda.current_stream()
     pipes = [wl, copy.copy(wl)]
-    pipes[1].setup_e2e(device)  # new buffers on the copy; the workload keeps its own
+    # new buffers and different inputs on the copy; the workload keeps its own
+    pipes[1].setup_e2e(device, seed=100)
     streams = [torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)]
 
     def run(n: int) -> None:
@@ -1127,6 +1196,70 @@ def time_e2e(wl, steps: int, dist: Dist, device: torch.device) -> dict:
     torch.cuda.synchronize()
     dist.barrier()
     return {"total_ms": e0.elapsed_time(e1), "pipelines": 2}
+
+
+def gather_outputs(wl, dist: Dist, reps: int = 5) -> dict | None:
+    """The optional all-gather of every rank's output block over NCCL (torch.distributed,
+    NVLink), timed on its own after the timed region: `reps` all-gathers of the workload's
+    gather_tensors() between CUDA events, max over ranks. Not part of `value`."""
+    if dist.world == 1 or not dist.pg or not hasattr(wl, "gather_tensors"):
+        return None
+    local = wl.gather_tensors()
+    bufs = [[torch.empty_like(t) for _ in range(dist.world)] for t in local]
+
+    def once() -> None:
+        for t, b in zip(local, bufs):
+            torch.distributed.all_gather(b, t)
+
+    once()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        once()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1) / reps)
+    nbytes = sum(t.numel() * t.element_size() for t in local)
+    ok = all(torch.equal(b[dist.rank], t) for t, b in zip(local, bufs))
+    return {"ms": round(ms, 4), "bytes_per_rank": nbytes,
+            "algbw_gbs": round(nbytes * dist.world / (ms * 1e6), 2),
+            "busbw_gbs": round(nbytes * (dist.world - 1) / (ms * 1e6), 2),
+            "own_block_intact": ok, "reps": reps,
+            "what": "torch.distributed.all_gather (NCCL) of each rank's output block"}
+
+
+def time_protocol(wl) -> dict:
+    """The reference's measurement protocol (src/kta/measure/protocol.py:27-45, the timing loop
+    of src/kta/measure/bench.py:124-192, kta_b200.measure.time_launches) on this workload's
+    own rotating device sets: before every launch its outputs are NaN-filled and a 2 x L2
+    flush buffer is written; each launch is timed alone between two CUDA events; warm-up
+    >= 10 iterations and 50 ms, measured >= 100 iterations and 200 ms; median with a bootstrap
+    95 % CI."""
+    from kta_b200 import measure
+
+    outs = [t for name in ("c", "o", "lse", "y") for t in (getattr(wl, name, None) or [])
+            if isinstance(t, torch.Tensor)]
+    nsets = getattr(wl, "nsets", NSETS)
+    res = measure.time_launches(wl.launch, outs, nsets, measure.V1, seed=0)
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    return {
+        "median_us": round(res["median_us"], 3),
+        "ci_low_us": round(res["ci_low_us"], 3),
+        "ci_high_us": round(res["ci_high_us"], 3),
+        "value_at_median": round(wl.work() / (res["median_us"] * 1e-6) / scale, 3),
+        "unit": wl.unit,
+        "n": res["n"],
+        "warmup_iters": res["warmup_iters"],
+        "input_sets": nsets,
+        "flush_bytes": res["flush_bytes"],
+        "protocol": "KTA measure protocol: NaN-filled outputs and a 2 x L2 flush before "
+                    "every launch, one launch between two CUDA events, warm-up >= 10 it and "
+                    "50 ms, >= 100 it and 200 ms, median + bootstrap 95% CI (1000 resamples)",
+    }
 
 
 def calibrate_cpu(wl, budget_s: float):
@@ -1228,6 +1361,18 @@ def run_kta(args, dist: Dist) -> dict | None:
         sus = pk["bf16_tflops_sustained"] * (2 if getattr(wl, "peak_key", None) == "fp8" else 1)
         roofline["peak_sustained"] = sus
         roofline["frac_of_sustained"] = round(achieved / sus, 4)
+    # the same K launches captured once as a CUDA graph and replayed back to back
+    graph_b2b = None
+    if not use_graph and not args.no_extra:
+        g = time_device_graph(wl, args.steps, args.warmup, dist)
+        g_ms = dist.max(g["total_ms"])
+        graph_b2b = {"value": round(world_work * args.steps / (g_ms / 1e3) / scale, 3),
+                     "unit": wl.unit, "ms_per_launch": round(g_ms / args.steps, 5),
+                     "launches": args.steps}
+    # the reference's own timing protocol on the same sets (this rank's figure)
+    protocol = None if args.no_extra else time_protocol(wl)
+    # the optional all-gather of the output blocks, timed on its own
+    gathered = None if args.no_extra else gather_outputs(wl, dist)
     # KTA's L1 speed-of-light bound of this rank's shard, as pct_of_bound
     cf = schemas.load_case_file(wl.case)
     hw = kbound.b200_model()
@@ -1254,7 +1399,7 @@ def run_kta(args, dist: Dist) -> dict | None:
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": wl.dtype_name,
-            "data": "synthetic (seeded N(0,1)/sqrt(K) per the case)",
+            "data": "synthetic: the case's distributions from a torch generator seeded with 0",
             "config": wl.config(dist.world),
             "impl": "kta",
             "roofline": roofline,
@@ -1272,6 +1417,9 @@ def run_kta(args, dist: Dist) -> dict | None:
             "cpu_baseline": cpu,
             "clocks": ck,
             "gpu_launches": args.steps,
+            "graph_b2b": graph_b2b,
+            "protocol": protocol,
+            "allgather": gathered,
         }
     return result
 
@@ -1313,7 +1461,7 @@ def run_reference(args, dist: Dist) -> dict | None:
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": wl.dtype_name,
-        "data": "synthetic (seeded N(0,1)/sqrt(K) per the case)",
+        "data": "synthetic: the case's distributions from a torch generator seeded with 0",
         "config": wl.config(1),
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads,
@@ -1333,6 +1481,8 @@ def main() -> int:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm_bf16_8192")
     ap.add_argument("--graph", action="store_true",
                     help="time the K steps as one CUDA graph replay (launch-bound workloads)")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the CUDA-graph back-to-back figure and the protocol median")
     ap.add_argument("--profile", action="store_true",
                     help="run W + K launches of the kernel only (the command for ncu captures)")
     args = ap.parse_args()

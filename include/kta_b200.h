@@ -4,10 +4,14 @@
  * Every entry is `extern "C"`, takes device pointers as `const void*` / `void*`, sizes as
  * int64_t and a CUDA stream as `void*` (NULL = the legacy default stream), returns a
  * kta_status code, and is asynchronous on that stream: no host synchronisation happens
- * inside. The caller owns every buffer (the library allocates no device memory on any
- * call path); the library keeps only per-device state: a 64-byte device status block
- * written by the kernels' watchdogs, and the resolved driver entry point for
- * cuTensorMapEncodeTiled. Entries are re-entrant across host threads and streams.
+ * inside. The caller owns every buffer it passes, and no entry allocates device memory when
+ * it is called. The library holds per-device state of its own: a 64-byte device status block
+ * written by the kernels' watchdogs, the resolved driver entry point for
+ * cuTensorMapEncodeTiled, and one fixed 8 MiB array of device memory (a file-scope
+ * __device__ array, held by every GPU that loads the library until the process exits) that
+ * only kta_decode_gqa_bf16_noalloc uses. Entries are re-entrant across host threads and
+ * streams, except kta_decode_gqa_bf16_noalloc: all its calls share that one array, so calls
+ * that overlap on the GPU race and must be serialised by the caller.
  *
  * Reference interfaces these entries replace (paths within kernel-template-agent):
  *   - src/kta/measure/bench.py:94-98 — a `BuiltModule(kind="so")` whose `entry` is called

@@ -219,8 +219,9 @@ def decode_gqa(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     kv_offsets[b] .. kv_offsets[b] + seqlens[b]; seqlens int32 [B], kv_offsets int64 [B].
     ``workspace`` (uint8, zero-initialised once) may be reused across calls on one stream.
     Without one, the library's own 8 MiB array is used when the split partials fit
-    (kta_decode_gqa_bf16_noalloc: no allocation, no extra kernel; calls that overlap on the
-    GPU then share it, so concurrent streams should pass their own workspace)."""
+    (kta_decode_gqa_bf16_noalloc: no allocation; the entry clears the array's arrival
+    counters with a memset on the stream before its kernel; calls that overlap on the GPU
+    share the array, so concurrent streams must pass their own workspace)."""
     _need_cuda(q, k_cache, v_cache, seqlens, kv_offsets)
     if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or \
             v_cache.dtype != torch.bfloat16:
@@ -256,7 +257,10 @@ def decode_gqa(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
 
 
 class _HostPipe:
-    """Device buffers and streams of one host-buffer GEMM shape, kept across calls."""
+    """Device buffers and streams of one host-buffer GEMM shape for one caller stream, kept
+    across calls. ``done`` marks the end of the last call's read-back: the next call's
+    uploads wait for it before they overwrite A and B, so a later call never changes the
+    buffers of one still in flight."""
 
     def __init__(self, m: int, n: int, k: int, dtype: torch.dtype, device: torch.device) -> None:
         self.a = torch.empty((m, k), dtype=dtype, device=device)
@@ -265,20 +269,31 @@ class _HostPipe:
         self.h2d = torch.cuda.Stream(device=device)
         self.comp = torch.cuda.Stream(device=device)
         self.d2h = torch.cuda.Stream(device=device)
+        self.done: torch.cuda.Event | None = None
 
 
 _PIPES: dict[tuple, _HostPipe] = {}
 
 
 def gemm_host(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
-              chunks: int = 8, device: torch.device | None = None) -> torch.Tensor:
+              chunks: int = 8, device: torch.device | None = None,
+              wait: bool = True) -> torch.Tensor:
     """C = A @ B.T with A, B and C in (pinned) host memory, end to end.
 
     The call copies B to the device, then A in ``chunks`` row blocks; each block's GEMM
     starts as soon as its rows have landed, and each block of C is copied back as soon as it
     is computed, on three streams, so host-device traffic in both directions overlaps the
-    tensor-core work. Returns once C is complete on the host. Device buffers are kept per
-    shape between calls."""
+    tensor-core work. The work is ordered after what the caller's current stream has queued,
+    and the caller's stream is ordered after the read-back.
+
+    With ``wait`` (the default) the call returns once C is complete on the host. With
+    ``wait=False`` it returns as soon as the work is queued: C is valid on the host once the
+    caller's current stream has reached this point (synchronise it, or an event recorded on
+    it), and A and B must stay unchanged until then.
+
+    Device buffers are kept per (shape, dtype, device, caller stream), so calls from
+    different streams never share them; consecutive calls from one stream reuse them in
+    order (each call's uploads wait for the previous call's read-back)."""
     if a.is_cuda or b.is_cuda:
         raise ValueError("gemm_host takes host tensors")
     m, k = a.shape
@@ -286,17 +301,19 @@ def gemm_host(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
     if kb != k or a.dtype != b.dtype:
         raise ValueError("A [M, K] and B [N, K] of one dtype")
     device = device or torch.device("cuda", torch.cuda.current_device())
-    key = (m, n, k, a.dtype, device)
+    caller = torch.cuda.current_stream(device)
+    key = (m, n, k, a.dtype, device, caller.cuda_stream)
     pipe = _PIPES.get(key)
     if pipe is None:
         pipe = _PIPES[key] = _HostPipe(m, n, k, a.dtype, device)
     if out is None:
         out = torch.empty((m, n), dtype=a.dtype, pin_memory=True)
-    caller = torch.cuda.current_stream(device)
     chunks = max(1, min(chunks, -(-m // 128)))
     rows = -(-m // chunks)
     rows = -(-rows // 128) * 128
     pipe.h2d.wait_stream(caller)
+    if pipe.done is not None:
+        pipe.h2d.wait_event(pipe.done)
     with torch.cuda.stream(pipe.h2d):
         pipe.b.copy_(b, non_blocking=True)
         b_ready = torch.cuda.Event()
@@ -320,5 +337,9 @@ def gemm_host(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
         for i, r0 in enumerate(range(0, m, rows)):
             pipe.d2h.wait_event(c_ready[i])
             out[r0:r0 + rows].copy_(pipe.c[r0:r0 + rows], non_blocking=True)
-    caller.wait_stream(pipe.d2h)
+        pipe.done = torch.cuda.Event()
+        pipe.done.record(pipe.d2h)
+    caller.wait_event(pipe.done)
+    if wait:
+        pipe.done.synchronize()
     return out

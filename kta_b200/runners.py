@@ -87,6 +87,23 @@ _TORCH = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32,
           "i8": torch.int8}
 
 
+def resolve(entry: str) -> Callable[..., dict[str, torch.Tensor]]:
+    """The runner of ``entry``: a libkta_b200 entry name from RUNNERS, or a plug-in runner
+    named ``"package.module:function"`` with the same ``(inputs, shape, outputs) -> outputs``
+    signature, imported on first use (so the checker can judge a caller's own launch code the
+    way the reference's checker judges any built module)."""
+    if entry in RUNNERS:
+        return RUNNERS[entry]
+    if ":" in entry:
+        import importlib
+
+        mod, _, name = entry.partition(":")
+        fn = getattr(importlib.import_module(mod), name, None)
+        if callable(fn):
+            return fn
+    raise ValueError(f"no runner for entry {entry!r}")
+
+
 def run(entry: str, problem: Problem, shape: dict[str, Any], data: dict[str, np.ndarray],
         nan_fill: bool = True, raw: bool = False, device: str = "cuda",
         launched: list[str] | None = None) -> dict[str, Any]:
@@ -96,8 +113,7 @@ def run(entry: str, problem: Problem, shape: dict[str, Any], data: dict[str, np.
     kernels)."""
     from kta_b200 import inputs as kinp
 
-    if entry not in RUNNERS:
-        raise ValueError(f"no runner for entry {entry!r}")
+    fn = resolve(entry)
     if "seqlens" in data and "max_seqlen" not in shape:
         shape = {**shape, "max_seqlen": int(np.max(data["seqlens"], initial=0))}
     dtypes = {t.name: t.dtype for t in problem.inputs}
@@ -110,14 +126,14 @@ def run(entry: str, problem: Problem, shape: dict[str, Any], data: dict[str, np.
             buf.view(torch.uint8).fill_(NAN_BYTE)
         outs[t.name] = buf
     if launched is None:
-        got = RUNNERS[entry](tens, shape, outs)
+        got = fn(tens, shape, outs)
         torch.cuda.synchronize()
     else:
         from torch.profiler import ProfilerActivity, profile
 
         torch.cuda.synchronize()
         with profile(activities=[ProfilerActivity.CUDA], acc_events=True) as prof:
-            got = RUNNERS[entry](tens, shape, outs)
+            got = fn(tens, shape, outs)
             torch.cuda.synchronize()
         launched.extend(ev.name for ev in prof.events() if ev.device_type.name == "CUDA"
                         and not ev.name.startswith(("Memset", "Memcpy")))

@@ -3,7 +3,7 @@
 Run in a container where the reference (kernel-template-agent) is checked out; it is not
 needed afterwards (the fixtures are committed):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the kernel-template-agent checkout>
 
 What it records, each from the reference itself:
 - inputs.npz: `kta.measure.inputs.generate` draws for every distribution of
@@ -317,4 +317,7 @@ def main(ref_root: str) -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <kernel-template-agent "
+                         "checkout>")
+    sys.exit(main(sys.argv[1]))

@@ -1,5 +1,7 @@
-"""GQA decode parity on the GPU: kta_decode_gqa_bf16 (through the C ABI) against the FP64
-oracle on identical bf16 inputs. Tolerance |y - ref| <= 1e-2 + 1e-2 |ref| (bf16 output)."""
+"""GQA decode parity on the GPU against the FP64 oracle on identical bf16 inputs, through both
+C-ABI entries: kta_decode_gqa_bf16 with a caller workspace ("workspace") and
+kta_decode_gqa_bf16_noalloc, whose partials live in the library's fixed array ("noalloc").
+Tolerance |y - ref| <= 1e-2 + 1e-2 |ref| (bf16 output)."""
 
 from __future__ import annotations
 
@@ -25,13 +27,24 @@ def _make(lengths, hq=32, hkv=8, d=128, seed=0, gap=0):
     return q, kc, vc, lengths, offsets
 
 
-def _run(dev, q, kc, vc, lengths, offsets, max_seqlen, workspace=None):
+ENTRIES = ["workspace", "noalloc"]
+
+
+def _run(dev, q, kc, vc, lengths, offsets, max_seqlen, workspace=None, entry="noalloc"):
+    """One decode through the C ABI. ``entry`` "workspace" passes a zeroed caller workspace
+    of kta_decode_workspace_bytes (kta_decode_gqa_bf16); "noalloc" passes none, which
+    ops.decode_gqa sends to kta_decode_gqa_bf16_noalloc when the partials fit its array."""
     from kta_b200 import ops
 
-    out = ops.decode_gqa(q.to(dev), kc.to(dev), vc.to(dev),
-                         torch.as_tensor(lengths, dtype=torch.int32).to(dev),
-                         torch.as_tensor(offsets, dtype=torch.int64).to(dev), max_seqlen,
-                         workspace=workspace)
+    bsz, hq, d = q.shape
+    if workspace is None and entry == "workspace":
+        need = ops.decode_workspace_bytes(bsz, hq, kc.shape[1], d, max_seqlen)
+        workspace = torch.zeros(max(need, 1), dtype=torch.uint8, device=dev)
+    out = torch.full(q.shape, float("nan"), dtype=torch.bfloat16, device=dev)
+    ops.decode_gqa(q.to(dev), kc.to(dev), vc.to(dev),
+                   torch.as_tensor(lengths, dtype=torch.int32).to(dev),
+                   torch.as_tensor(offsets, dtype=torch.int64).to(dev), max_seqlen,
+                   out=out, workspace=workspace)
     torch.cuda.synchronize()
     return out
 
@@ -47,42 +60,47 @@ def _check(out, q, kc, vc, lengths, offsets):
     assert not bad.any(), f"{int(bad.sum())} mismatches, max err {err.max():.3e}"
 
 
+@pytest.mark.parametrize("entry", ENTRIES)
 @pytest.mark.parametrize("lengths", [[1], [7, 128, 129], [512, 513, 1024, 1025],
                                      [100, 2000, 4096, 3333, 1, 640]])
-def test_decode_small(cuda_device, lengths):
+def test_decode_small(cuda_device, lengths, entry):
     q, kc, vc, ln, off = _make(lengths)
-    out = _run(cuda_device, q, kc, vc, ln, off, max(lengths))
+    out = _run(cuda_device, q, kc, vc, ln, off, max(lengths), entry=entry)
     _check(out, q, kc, vc, ln, off)
 
 
+@pytest.mark.parametrize("entry", ENTRIES)
 @pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 8), (32, 4), (64, 4), (4, 1)])
-def test_decode_group_sizes(cuda_device, hq, hkv):
+def test_decode_group_sizes(cuda_device, hq, hkv, entry):
     q, kc, vc, ln, off = _make([300, 1500, 77], hq=hq, hkv=hkv)
-    out = _run(cuda_device, q, kc, vc, ln, off, 2048)
+    out = _run(cuda_device, q, kc, vc, ln, off, 2048, entry=entry)
     _check(out, q, kc, vc, ln, off)
 
 
+@pytest.mark.parametrize("entry", ENTRIES)
 @pytest.mark.parametrize("lengths", [[8192], [300], [8192, 8192, 17], [1] * 40])
-def test_decode_splits_across_ctas(cuda_device, lengths):
+def test_decode_splits_across_ctas(cuda_device, lengths, entry):
     """One long sequence spread over many CTAs (its pairs split and combined), and fewer
     tiles than CTAs (CTAs with empty ranges must not be counted as contributors)."""
     q, kc, vc, ln, off = _make(lengths)
-    out = _run(cuda_device, q, kc, vc, ln, off, max(lengths))
+    out = _run(cuda_device, q, kc, vc, ln, off, max(lengths), entry=entry)
     _check(out, q, kc, vc, ln, off)
 
 
-def test_decode_gaps_between_sequences(cuda_device):
+@pytest.mark.parametrize("entry", ENTRIES)
+def test_decode_gaps_between_sequences(cuda_device, entry):
     """Sequences need not be packed back to back: rows between them are never read."""
     q, kc, vc, ln, off = _make([700, 513, 2], gap=37)
-    out = _run(cuda_device, q, kc, vc, ln, off, 1024)
+    out = _run(cuda_device, q, kc, vc, ln, off, 1024, entry=entry)
     _check(out, q, kc, vc, ln, off)
 
 
-def test_decode_baseline_config(cuda_device):
+@pytest.mark.parametrize("entry", ENTRIES)
+def test_decode_baseline_config(cuda_device, entry):
     """B=64, Hq=32, Hkv=8, D=128, lengths uniform in [1024, 8192] from seed 0."""
     lengths = np.random.default_rng(0).integers(1024, 8193, size=64)
     q, kc, vc, ln, off = _make(lengths)
-    out = _run(cuda_device, q, kc, vc, ln, off, 8192)
+    out = _run(cuda_device, q, kc, vc, ln, off, 8192, entry=entry)
     _check(out, q, kc, vc, ln, off)
 
 

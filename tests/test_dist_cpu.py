@@ -1,6 +1,6 @@
 """Multi-rank host logic of bench.py on CPU: world_size 2 over gloo (127.0.0.1). Each
-rank derives its shard of the GEMM's N columns and its decode sequences by LPT with no
-communication; together the shards cover the work exactly once; the max / sum reductions
+rank derives its shard of the GEMM's N columns, its attention (batch, head) pairs and its
+decode sequences by LPT with no communication; together the shards cover the work exactly once; the max / sum reductions
 over ranks (the bench's timing and throughput) agree on every rank; a rank that raises is
 reported on the host and the others end with an error instead of hanging."""
 
@@ -36,11 +36,13 @@ def _worker(rank: int, world: int, port: int, out: dict, fail_rank: int) -> None
             raise RuntimeError("planted failure on the host")
         lo, hi = bench.shard(8192, world, rank, align=128)
         dec = bench.DecodeWorkload(d)
+        att = bench.AttnWorkload(d)
         d.barrier()
         mx = d.max(float(rank + 1))
         sm = d.sum(float(hi - lo))
         out[rank] = {"cols": (lo, hi), "seqs": sorted(dec.lengths), "tokens": dec.tokens,
-                     "max": mx, "sum": sm}
+                     "max": mx, "sum": sm,
+                     "attn": (att.pair_lo, att.pair_hi, att.b, att.hh, att.flops)}
     finally:
         d.close()
 
@@ -78,6 +80,13 @@ def test_two_ranks_shard_without_collective_and_reduce_timings():
     t0, t1 = out[0]["tokens"], out[1]["tokens"]
     assert abs(t0 - t1) <= 8192  # LPT balance within one sequence
     assert bench.lpt([5, 4, 3, 3], 2) in ([[0, 3], [1, 2]], [[1, 2], [0, 3]])
+    # attention: (batch, head) pairs split into whole batch entries, together every pair once,
+    # equal causal work on both ranks
+    (lo0, hi0, b0, h0, f0), (lo1, hi1, b1, h1, f1) = out[0]["attn"], out[1]["attn"]
+    assert (lo0, hi0, lo1, hi1) == (0, 128, 128, 256)
+    assert (b0, h0) == (b1, h1) == (4, 32)
+    full = bench.AttnWorkload(bench.Dist(1, backend="gloo"))
+    assert f0 == f1 and f0 + f1 == full.flops
 
 
 @pytest.mark.timeout(300)

@@ -110,6 +110,74 @@ def test_gemm_bf16_8192_sampled_rows(cuda_device):
     assert torch.isfinite(c.float()).all()
 
 
+# Shapes the default routing sends to the 2-SM pair kernel (256x256 tiles over CTA pairs):
+# pair tiles >= SMs / 2 and no more waves than 128x256 tiles on 148 SMs, e.g. 3000 x 2900:
+# 12 x 12 = 144 pair tiles (2 waves of 74) against 24 x 12 = 288 one-SM tiles (2 waves of 148).
+# Every one has ragged M and N (not multiples of 256) and most a K tail (not a multiple of 64).
+PAIR_SHAPES = [
+    (3000, 2900, 1000),
+    (2304, 4352, 264),
+    (4100, 2600, 1032),
+    (2200, 2312, 72),
+]
+
+
+@pytest.mark.parametrize("route", ["default", "force"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
+def test_gemm_pair_kernel_ragged(cuda_device, monkeypatch, m, n, k, dtype, route):
+    """The 2-SM pair kernel on ragged edges, by the default routing and with
+    KTA_GEMM_PAIR=force (read on every call)."""
+    from kta_b200 import ops
+
+    if route == "force":
+        monkeypatch.setenv("KTA_GEMM_PAIR", "force")
+    else:
+        monkeypatch.delenv("KTA_GEMM_PAIR", raising=False)
+    a, b = _inputs(m, n, k, dtype, seed=3)
+    c = torch.full((m, n), float("nan"), dtype=dtype, device=cuda_device)
+    ops.gemm(a.to(cuda_device), b.to(cuda_device), out=c)
+    torch.cuda.synchronize()
+    _check(c, ogemm.gemm_tn(a.double().numpy(), b.double().numpy()))
+
+
+@pytest.mark.parametrize("route", ["force", "off"])
+@pytest.mark.parametrize("m,n,k", [(520, 1000, 136), (129, 384, 64), (700, 904, 320)])
+def test_gemm_small_shapes_on_both_kernels(cuda_device, monkeypatch, m, n, k, route):
+    """Shapes the default routing keeps on the 1-SM kernel, forced onto the pair kernel
+    (M > 128), and the pair kernel switched off."""
+    from kta_b200 import ops
+
+    monkeypatch.setenv("KTA_GEMM_PAIR", route if route == "force" else "0")
+    a, b = _inputs(m, n, k, torch.bfloat16, seed=4)
+    c = ops.gemm(a.to(cuda_device), b.to(cuda_device))
+    torch.cuda.synchronize()
+    _check(c, ogemm.gemm_tn(a.double().numpy(), b.double().numpy()))
+
+
+@pytest.mark.parametrize("route", ["default", "force", "off"])
+def test_gemm_8192_with_k_tail_sampled_rows(cuda_device, monkeypatch, route):
+    """8192 x 8192 x 8200: the headline shape with a K tail of 8 (not a multiple of the 64-deep
+    stage) on the pair kernel (default and forced) and on the 1-SM kernel; 100 sampled rows
+    against FP64."""
+    from kta_b200 import ops
+
+    if route == "default":
+        monkeypatch.delenv("KTA_GEMM_PAIR", raising=False)
+    else:
+        monkeypatch.setenv("KTA_GEMM_PAIR", "force" if route == "force" else "0")
+    m, n, k = 8192, 8192, 8200
+    a, b = _inputs(m, n, k, torch.bfloat16, seed=6)
+    c = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    ops.gemm(a.to(cuda_device), b.to(cuda_device), out=c)
+    torch.cuda.synchronize()
+    rows = np.random.default_rng(2).choice(m, size=96, replace=False)
+    rows = np.concatenate([rows, [0, 255, 256, m - 1]])
+    ref = ogemm.gemm_tn_rows(a.double().numpy(), b.double().numpy(), rows)
+    _check(c[torch.as_tensor(rows)], ref)
+    assert not torch.isnan(c.float()).any()
+
+
 def test_gemm_is_deterministic(cuda_device):
     from kta_b200 import ops
 
@@ -150,3 +218,33 @@ def test_gemm_host_buffers_pipelined(cuda_device, m, n, k, chunks):
     torch.cuda.synchronize()
     assert not c.is_cuda
     _check(c, ogemm.gemm_tn(a.double().numpy(), b.double().numpy()))
+
+
+def test_gemm_host_returns_with_c_on_the_host(cuda_device):
+    """With the default wait=True the result is complete on return: read at once, no sync."""
+    from kta_b200 import ops
+
+    a, b = _inputs(1536, 1024, 512, torch.bfloat16, seed=8)
+    c = ops.gemm_host(a.pin_memory(), b.pin_memory())
+    _check(c, ogemm.gemm_tn(a.double().numpy(), b.double().numpy()))
+
+
+def test_gemm_host_two_streams_in_flight_with_different_inputs(cuda_device):
+    """Four calls in flight at once, alternating between two caller streams, each with its own
+    inputs and output (wait=False): each stream gets device buffers of its own and consecutive
+    calls on one stream reuse them only after the previous read-back, so no call reads or
+    returns another call's data."""
+    from kta_b200 import ops
+
+    m, n, k = 2048, 1536, 1024
+    sets = [_inputs(m, n, k, torch.bfloat16, seed=20 + i) for i in range(4)]
+    pinned = [(a.pin_memory(), b.pin_memory()) for a, b in sets]
+    outs = [torch.full((m, n), float("nan"), dtype=torch.bfloat16).pin_memory()
+            for _ in range(4)]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for i in range(4):
+        with torch.cuda.stream(streams[i % 2]):
+            ops.gemm_host(*pinned[i], out=outs[i], wait=False)
+    torch.cuda.synchronize()
+    for (a, b), c in zip(sets, outs):
+        _check(c, ogemm.gemm_tn(a.double().numpy(), b.double().numpy()))
