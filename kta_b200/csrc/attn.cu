@@ -413,8 +413,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         __syncwarp();
       };
+      // O_t of the previous unit must have been read by its epilogue before the first PV of
+      // tile t overwrites it; the S MMAs of the new unit do not touch O and go ahead of that
+      auto wait_o_free = [&](int tile) -> bool {
+        if (units_done == 0) return true;
+        if (!mbar_wait(&o_free[tile], ofree_phase[tile], abort_flag, p.status, SITE_MMA_OFREE)) {
+          return false;
+        }
+        ofree_phase[tile] ^= 1u;
+        tc_fence_after();
+        return true;
+      };
       auto issue_pv = [&](int tile, uint64_t vdesc, bool first, uint64_t* done0,
                           uint64_t* done1) -> bool {
+        if (first && !wait_o_free(tile)) return false;
         // P arrives in two halves (keys 0-63, 64-127): the first half of PV starts while the
         // softmax still works on the second
 #pragma unroll
@@ -445,16 +457,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const Unit un = unit_of(u, p);
         if (!mbar_wait(q_full, qphase, abort_flag, p.status, SITE_MMA_Q)) break;
         qphase ^= 1u;
-        // O_A / O_B of the previous unit must have been read by its epilogue
-        if (units_done > 0) {
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (!mbar_wait(&o_free[t], ofree_phase[t], abort_flag, p.status, SITE_MMA_OFREE)) {
-              ok = false;
-            }
-            ofree_phase[t] ^= 1u;
-          }
-          if (!ok) break;
-        }
         tc_fence_after();
         const int a_last = 2 * un.pair;  // tile A's diagonal KV tile
         uint64_t prev_vdesc = 0;
@@ -504,7 +506,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
         } else {
-          if (elect_one_sync()) umma_commit(&o_done[1]);  // tile B absent: hand O_B back
+          // tile B absent: hand O_B back once the previous unit's epilogue has read it
+          if (!wait_o_free(1)) break;
+          if (elect_one_sync()) umma_commit(&o_done[1]);
           __syncwarp();
         }
         ++units_done;

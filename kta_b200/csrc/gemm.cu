@@ -63,15 +63,23 @@ struct Layout {
   static_assert(ALLOC <= 232448, "shared memory budget of one sm_100 CTA");
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb,
-                                            int& nb) {
-  const int per_group = GROUP_M * tiles_n;
+// Tile `tile` of a grouped raster: bands of `group_m` tile rows, each band walked column by
+// column (a column's group_m tiles are consecutive), so the tiles in flight share a band of
+// A panels and a few B panels.
+__device__ __forceinline__ void tile_coords_g(int tile, int tiles_m, int tiles_n, int group_m,
+                                              int& mb, int& nb) {
+  const int per_group = group_m * tiles_n;
   const int group = tile / per_group;
-  const int first_m = group * GROUP_M;
-  const int gsz = min(tiles_m - first_m, GROUP_M);
+  const int first_m = group * group_m;
+  const int gsz = min(tiles_m - first_m, group_m);
   const int r = tile - group * per_group;
   mb = first_m + r % gsz;
   nb = r / gsz;
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb,
+                                            int& nb) {
+  tile_coords_g(tile, tiles_m, tiles_n, GROUP_M, mb, nb);
 }
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -315,8 +323,8 @@ struct PairLayout {
 template <bool BF16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
-                     unsigned int* status) {
+                     const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int group_m,
+                     int l2_hint, unsigned int* status) {
   using L = PairLayout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -377,9 +385,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // the band's A panels are read again by the next columns' tiles: keep them in L2 ahead
+      // of B, whose panels serve only the tiles of one column
+      const uint64_t pol_a = l2_policy_evict_last();
+      const uint64_t pol_b = l2_policy_evict_first();
       for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
         int mb, nb;
-        tile_coords(tile, tiles_m, tiles_n, mb, nb);
+        tile_coords_g(tile, tiles_m, tiles_n, group_m, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, SITE_PRODUCER_EMPTY)) {
             ok = false;
@@ -387,10 +399,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           const uint32_t bar0 = peer_addr(&full[stage], 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (L::A_BYTES + L::B_BYTES));
-          tma_load_2d_pair(&tmA, bar0, smem + L::OFF_A + stage * L::A_BYTES, kb * BK,
-                           mb * P_BM + static_cast<int>(rank) * 128);
-          tma_load_2d_pair(&tmB, bar0, smem + L::OFF_B + stage * L::B_BYTES, kb * BK,
-                           nb * P_BN + static_cast<int>(rank) * 128);
+          uint8_t* da = smem + L::OFF_A + stage * L::A_BYTES;
+          uint8_t* db = smem + L::OFF_B + stage * L::B_BYTES;
+          const int ya = mb * P_BM + static_cast<int>(rank) * 128;
+          const int yb = nb * P_BN + static_cast<int>(rank) * 128;
+          if (l2_hint) {
+            tma_load_2d_pair_hint(&tmA, bar0, da, kb * BK, ya, pol_a);
+            tma_load_2d_pair_hint(&tmB, bar0, db, kb * BK, yb, pol_b);
+          } else {
+            tma_load_2d_pair(&tmA, bar0, da, kb * BK, ya);
+            tma_load_2d_pair(&tmB, bar0, db, kb * BK, yb);
+          }
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -448,7 +467,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t tempty0[2] = {peer_addr(&tempty[0], 0), peer_addr(&tempty[1], 0)};
     for (int tile = pair; tile < num_tiles; tile += pairs) {
       int mb, nb;
-      tile_coords(tile, tiles_m, tiles_n, mb, nb);
+      tile_coords_g(tile, tiles_m, tiles_n, group_m, mb, nb);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, status, SITE_EPI_TFULL)) break;
       tc_fence_after();
       const uint32_t t_row =
@@ -832,6 +851,18 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
                    device_status_ptr());
 }
 
+// Raster of the pair kernel: bands of P_GROUP_M tile rows (8 x 256 rows: a 32 MB band of A
+// for K = 8192, which stays in L2 under the evict-last policy while B streams past it);
+// KTA_GEMM_GROUP=<n> and KTA_GEMM_L2HINT=0 override both (tuning runs).
+constexpr int P_GROUP_M = 8;
+inline void pair_raster_env(int& group_m, int& l2_hint) {
+  if (const char* g = std::getenv("KTA_GEMM_GROUP")) {
+    const int v = std::atoi(g);
+    if (v >= 1 && v <= 64) group_m = v;
+  }
+  if (const char* h = std::getenv("KTA_GEMM_L2HINT")) l2_hint = h[0] != '0';
+}
+
 template <bool BF16>
 int launch_pair(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda,
                 int64_t ldb, int64_t ldc, cudaStream_t stream) {
@@ -865,8 +896,10 @@ int launch_pair(const void* A, const void* B, void* C, int M, int N, int K, int6
   if (s != KTA_OK) return s;
   const int tiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
   const int pairs = std::max(1, std::min(tiles, current_sm_count() / 2));
+  int group_m = P_GROUP_M, l2_hint = 1;
+  pair_raster_env(group_m, l2_hint);
   return launch_ex(kernel, dim3(static_cast<unsigned>(2 * pairs)), dim3(NUM_THREADS), L::ALLOC,
-                   stream, 2, ta, tb, tc, M, N, K, device_status_ptr());
+                   stream, 2, ta, tb, tc, M, N, K, group_m, l2_hint, device_status_ptr());
 }
 
 // Estimated relative time of a tile width: waves x columns, discounted by how close the

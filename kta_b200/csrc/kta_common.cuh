@@ -478,6 +478,17 @@ __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_
       : "memory");
 }
 
+// The same load with an L2 eviction-priority policy (createpolicy) for the fetched lines.
+__device__ __forceinline__ void tma_load_2d_pair_hint(const CUtensorMap* map, uint32_t bar_cluster,
+                                                      void* dst, int32_t x, int32_t y,
+                                                      uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                               uint32_t idesc, uint32_t accumulate) {
   asm volatile(

@@ -31,18 +31,19 @@ def test_dropped_row_fails_numeric(cuda_device):
     res = checkflow.quick_check(cf, GEMM_SHAPE, entry=PLANTED + "gemm_row_dropped")
     assert not res["passed"]
     bad = _failed(res, "numeric")
-    assert bad, res["failures"]
+    assert bad and all("error" not in f for f in bad), res["failures"]
     # the unwritten row shows as non-finite elements: the NaN-fill coverage check
     assert any(f.get("nonfinite_where_ref_finite", 0) >= GEMM_SHAPE["N"] for f in bad), bad
-    assert res["sub_checks"]["anticheat"] is True  # only library kernels ran
+    assert res["sub_checks"].get("anticheat") is True, res["failures"]  # library kernels only
 
 
 def test_wrong_fp8_weight_scale_fails_numeric(cuda_device):
     cf = schemas.load_case_file("gemm_fp8_blockscaled")
     res = checkflow.quick_check(cf, GEMM_SHAPE, entry=PLANTED + "fp8_scale_doubled")
     assert not res["passed"]
-    assert _failed(res, "numeric"), res["failures"]
-    assert res["sub_checks"]["anticheat"] is True
+    assert res["sub_checks"].get("anticheat") is True, res["failures"]
+    bad = _failed(res, "numeric")
+    assert bad and all("error" not in f for f in bad), res["failures"]
 
 
 def test_foreign_kernel_fails_anticheat(cuda_device):
@@ -50,8 +51,8 @@ def test_foreign_kernel_fails_anticheat(cuda_device):
     res = checkflow.quick_check(cf, GEMM_SHAPE, entry=PLANTED + "gemm_with_foreign_kernel")
     assert not res["passed"]
     bad = _failed(res, "anticheat.kernels")
-    assert bad and all("undeclared kernel" in f["detail"] for f in bad), res["failures"]
-    assert res["sub_checks"]["numeric"] is True  # the numbers themselves are right
+    assert bad and all("undeclared kernel" in f.get("detail", "") for f in bad), res["failures"]
+    assert res["sub_checks"].get("numeric") is True, res["failures"]  # the numbers are right
 
 
 def test_nondeterministic_runner_fails_anticheat(cuda_device):

@@ -158,3 +158,70 @@ def test_e2m1_decode_is_the_e2m1_table():
 
     vals = dequant.decode(np.arange(16), "e2m1")
     assert list(vals) == [0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.0, -0.5, -1, -1.5, -2, -3, -4, -6]
+
+
+# ---- pins to the reference's own kernels (tests/golden/kernels.npz, made on a B200 by
+# ---- tests/golden/make_kernel_golden.py from KTA's TileLang test-set kernels) -------------
+@pytest.fixture(scope="module")
+def kz():
+    return np.load(GOLDEN / "kernels.npz")
+
+
+def _f16(bits):
+    return numerics.f16_bits_to_f64(np.asarray(bits))
+
+
+def test_attention_oracle_matches_the_reference_fa_forward_kernel(kz):
+    """KTA's fa_forward (perfmodel/testset/gen.py:417-486: online softmax in exp2 form, P in
+    f16, f16 output) against the oracle's non-causal attention in FP64 on the same f16 inputs:
+    within the kernel's own f16 roundings. The causal oracle differs from it by far more, so
+    the pin tells the two functions apart."""
+    b, s, h, d = (int(x) for x in kz["fa.shape"])
+    q, k, v = (_f16(kz[n]).reshape(b, s, h, d) for n in ("fa.Q", "fa.K", "fa.V"))
+    y = _f16(kz["fa.Out"]).reshape(b, s, h, d)
+    o, _ = oatt.attn_fwd(q, k, v, d ** -0.5, causal=False)
+    err = np.abs(y - o)
+    assert np.isfinite(y).all()
+    assert np.all(err <= 2e-3 + 2e-3 * np.abs(o)), err.max()
+    oc, _ = oatt.attn_fwd(q, k, v, d ** -0.5, causal=True)
+    assert np.abs(y - oc).max() > 0.05
+    # the last query row sees every key under the causal mask too
+    np.testing.assert_array_less(np.abs(y[:, -1] - oc[:, -1]), 2e-3 + 2e-3 * np.abs(oc[:, -1]))
+
+
+def test_decode_oracle_matches_the_reference_split_and_combine_kernels(kz):
+    """KTA's decode_partial (gen.py:493-560) and decode_combine (gen.py:563-590): the oracle's
+    per-chunk partials and log2-unit LSE against the split kernel's f16 outputs, the oracle's
+    combine of the kernel's own partials against the combine kernel's output, and the oracle's
+    whole decode against it."""
+    b, hq, hkv, s, d, split = (int(x) for x in kz["dec.shape"])
+    q = _f16(kz["dec.Q"]).reshape(b, hq, d)
+    k = _f16(kz["dec.K"]).reshape(b, s, hkv, d)
+    v = _f16(kz["dec.V"]).reshape(b, s, hkv, d)
+    glse = _f16(kz["dec.glse"]).reshape(b, hq, split)
+    opart = _f16(kz["dec.Opart"]).reshape(b, hq, split, d)
+    out = _f16(kz["dec.Out"]).reshape(b, hq, d)
+    parts, lse2 = oatt.decode_partials(q[0], k[0], v[0], s, 0, d ** -0.5, s // split)
+    assert np.all(np.abs(glse[0] - lse2) <= 1e-2 + 1e-3 * np.abs(lse2)), \
+        np.abs(glse[0] - lse2).max()
+    assert np.all(np.abs(opart[0] - parts) <= 2e-3 + 2e-3 * np.abs(parts)), \
+        np.abs(opart[0] - parts).max()
+    comb = oatt.decode_combine(opart[0], glse[0])
+    assert np.all(np.abs(out[0] - comb) <= 1e-3 + 1e-3 * np.abs(comb)), np.abs(out[0] - comb).max()
+    full = oatt.decode_gqa(q, k[0], v[0], np.array([s]), np.array([0]), d ** -0.5)
+    assert np.all(np.abs(out - full) <= 2e-3 + 2e-3 * np.abs(full)), np.abs(out - full).max()
+
+
+def test_fp8_oracle_matches_the_reference_fp8gemm_kernel(kz):
+    """KTA's fp8gemm (gen.py:306-329: C = A B^T in e4m3, fp32 accumulate, f16 out) against the
+    oracle's block-scaled statement with every scale 1 (the unscaled special case), on the same
+    codes: within the f16 rounding of C."""
+    m, n, kk = (int(x) for x in kz["fp8.shape"])
+    a = np.asarray(kz["fp8.A"]).reshape(m, kk)
+    bb = np.asarray(kz["fp8.B"]).reshape(n, kk)
+    c = _f16(kz["fp8.C"]).reshape(m, n)
+    nb = -(-kk // 128)
+    ref = ofp8.gemm_blockscaled(a, np.ones((m, nb), np.float32), bb,
+                                np.ones((-(-n // 128), nb), np.float32))
+    err = np.abs(c - ref)
+    assert np.all(err <= 1e-3 * np.abs(ref) + 1e-2), err.max()
