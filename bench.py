@@ -59,6 +59,9 @@ def sets_for(bytes_per_set: float) -> int:
 
 
 CPU_BUDGET_S = 12.0  # CPU baseline sample: about this much host compute
+# Back-to-back launches before every timed region: the SM clock under the 1 kW power cap
+# settles within about a second of sustained load; timing earlier catches a transient.
+PREHEAT_S = 2.0
 
 
 # ---------------------------------------------------------------------------------------
@@ -1100,11 +1103,12 @@ def time_device(wl, steps: int, warmup: int, dist: Dist) -> dict:
     stream = torch.cuda.current_stream()
     for i in range(warmup):
         wl.launch(i)
-    # keep the GPU busy for ~0.5 s more so clocks settle and the sampler is running
+    # keep the GPU busy for PREHEAT_S more, back to back, so that the clock has settled under
+    # the power cap before the timed launches (the sustained regime, not a transient)
     torch.cuda.synchronize()
     t_w = time.perf_counter()
     i = 0
-    while time.perf_counter() - t_w < 0.5:
+    while time.perf_counter() - t_w < PREHEAT_S:
         wl.launch(i)
         i += 1
         if i % 8 == 0:
@@ -1143,7 +1147,7 @@ def time_device_graph(wl, steps: int, warmup: int, dist: Dist) -> dict:
     torch.cuda.synchronize()
     graph.replay()  # warm replay
     t_w = time.perf_counter()
-    while time.perf_counter() - t_w < 0.5:
+    while time.perf_counter() - t_w < PREHEAT_S:
         graph.replay()
         torch.cuda.synchronize()
     dist.barrier()
@@ -1351,8 +1355,9 @@ def run_kta(args, dist: Dist) -> dict | None:
         "algorithmic_bytes_per_launch": wl.bytes,
         "algorithmic_flops_per_launch": getattr(wl, "flops", None),
         "mean_launch_ms": round(mean_launch_ms, 5),
-        "timing": "one CUDA graph of the K launches, total / K" if use_graph else
-                  "CUDA events between consecutive launches on the launching stream",
+        "timing": ("one CUDA graph of the K launches, total / K" if use_graph else
+                   "CUDA events between consecutive launches on the launching stream")
+                  + f", after {PREHEAT_S:.1f} s of back-to-back launches",
         "median_launch_ms": round(statistics.median(per), 5),
     }
     if wl.unit == "TFLOP/s" and pk["bf16_tflops_sustained"] > 0:

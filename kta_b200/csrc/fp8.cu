@@ -21,7 +21,6 @@
 //   * every mbarrier wait is bounded.
 #include <algorithm>
 #include <cmath>
-#include <cstdlib>
 
 #include "kta_common.cuh"
 #include "kta_host.h"
@@ -78,10 +77,7 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = r / gsz;
 }
 
-// PCH: accumulator columns each promotion warp loads from TMEM per tcgen05.ld (16 or 32);
-// fewer, wider loads put fewer load-latency waits on each warp's path through a K block.
-template <int PCH>
-__global__ void __maxnreg__(112)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -221,17 +217,13 @@ __global__ void __maxnreg__(112)
         const uint32_t t = tmem + lane_base + buf * BN + cg * PROMO_COLS;
         const uint64_t s2 = f2(scale, scale);
 #pragma unroll
-        for (int c = 0; c < PROMO_COLS; c += PCH) {
-          uint32_t r[PCH];
-          if constexpr (PCH == 32) {
-            tmem_ld_32x32b_x32(t + c, r);
-          } else {
-            tmem_ld_32x32b_x16(t + c, r);
-          }
+        for (int c = 0; c < PROMO_COLS; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t + c, r);
           tmem_ld_wait();
           reg_fence(r);
 #pragma unroll
-          for (int i = 0; i < PCH / 2; ++i) {
+          for (int i = 0; i < 8; ++i) {
             acc[c / 2 + i] = fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), s2,
                                   acc[c / 2 + i]);
           }
@@ -312,18 +304,12 @@ int launch(const void* A, const void* sa, const void* B, const void* sb, void* C
   prm.KB = (K + BK - 1) / BK;
   prm.NB = (N + 127) / 128;
   prm.status = device_status_ptr();
+  s = set_kernel_smem(reinterpret_cast<const void*>(fp8_gemm_kernel), Layout::ALLOC);
+  if (s != KTA_OK) return s;
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, current_sm_count()));
-  // KTA_FP8_CHUNK=16|32 picks the promotion load width (tuning runs); 32 by default
-  int chunk = 32;
-  if (const char* e = std::getenv("KTA_FP8_CHUNK")) chunk = std::atoi(e) == 16 ? 16 : 32;
-  auto go = [&](auto kernel) -> int {
-    int st = set_kernel_smem(reinterpret_cast<const void*>(kernel), Layout::ALLOC);
-    if (st != KTA_OK) return st;
-    return launch_ex(kernel, dim3(grid), dim3(NUM_THREADS), Layout::ALLOC, stream, 1, ta, tb,
-                     prm);
-  };
-  return chunk == 16 ? go(fp8_gemm_kernel<16>) : go(fp8_gemm_kernel<32>);
+  return launch_ex(fp8_gemm_kernel, dim3(grid), dim3(NUM_THREADS), Layout::ALLOC, stream, 1, ta,
+                   tb, prm);
 }
 
 }  // namespace fp8

@@ -403,11 +403,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* db = smem + L::OFF_B + stage * L::B_BYTES;
           const int ya = mb * P_BM + static_cast<int>(rank) * 128;
           const int yb = nb * P_BN + static_cast<int>(rank) * 128;
-          if (l2_hint) {
+          if (l2_hint & 1) {
             tma_load_2d_pair_hint(&tmA, bar0, da, kb * BK, ya, pol_a);
-            tma_load_2d_pair_hint(&tmB, bar0, db, kb * BK, yb, pol_b);
           } else {
             tma_load_2d_pair(&tmA, bar0, da, kb * BK, ya);
+          }
+          if (l2_hint & 2) {
+            tma_load_2d_pair_hint(&tmB, bar0, db, kb * BK, yb, pol_b);
+          } else {
             tma_load_2d_pair(&tmB, bar0, db, kb * BK, yb);
           }
           if (++stage == P_STAGES) {
@@ -465,6 +468,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc_phase = 0;
     int buf = 0;
     const uint32_t tempty0[2] = {peer_addr(&tempty[0], 0), peer_addr(&tempty[1], 0)};
+    // C is written once and never read back here: its lines should not push A panels out
+    const uint64_t pol_c = l2_policy_evict_first();
     for (int tile = pair; tile < num_tiles; tile += pairs) {
       int mb, nb;
       tile_coords_g(tile, tiles_m, tiles_n, group_m, mb, nb);
@@ -504,7 +509,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, sbuf, nb * P_BN + c * EPI_COLS, row0);
+          if (l2_hint & 4) {
+            tma_store_2d_hint(&tmC, sbuf, nb * P_BN + c * EPI_COLS, row0, pol_c);
+          } else {
+            tma_store_2d(&tmC, sbuf, nb * P_BN + c * EPI_COLS, row0);
+          }
           bulk_commit_group();
         }
         buf ^= 1;
@@ -853,14 +862,15 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
 
 // Raster of the pair kernel: bands of P_GROUP_M tile rows (8 x 256 rows: a 32 MB band of A
 // for K = 8192, which stays in L2 under the evict-last policy while B streams past it);
-// KTA_GEMM_GROUP=<n> and KTA_GEMM_L2HINT=0 override both (tuning runs).
+// KTA_GEMM_GROUP=<n> and KTA_GEMM_L2HINT=<bits> override both (tuning runs; bit 0: A
+// loads evict-last, bit 1: B loads evict-first, bit 2: C stores evict-first).
 constexpr int P_GROUP_M = 8;
 inline void pair_raster_env(int& group_m, int& l2_hint) {
   if (const char* g = std::getenv("KTA_GEMM_GROUP")) {
     const int v = std::atoi(g);
     if (v >= 1 && v <= 64) group_m = v;
   }
-  if (const char* h = std::getenv("KTA_GEMM_L2HINT")) l2_hint = h[0] != '0';
+  if (const char* h = std::getenv("KTA_GEMM_L2HINT")) l2_hint = std::atoi(h) & 7;
 }
 
 template <bool BF16>

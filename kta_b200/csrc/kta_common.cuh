@@ -172,6 +172,16 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
       : "memory");
 }
 
+// The same store with an L2 eviction-priority policy for the written lines.
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, const void* src, int32_t x,
+                                                  int32_t y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint"
+      " [%0, {%2, %3}], [%1], %4;" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int32_t x,
                                              int32_t y, int32_t z) {
   asm volatile(

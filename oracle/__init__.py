@@ -19,7 +19,11 @@ Contents, each citing the reference code it restates (paths within kernel-templa
 Pinning: tests/golden holds fixtures generated in a container where the reference's Python
 is importable (tests/golden/make_golden.py): the reference's own input generators, its own
 ref_torch.py run on the CPU, and its compare_output / library_verdict / bound. The oracle is
-checked against them in tests/test_oracle_golden.py. Attention and block-scaled FP8 have no
-reference implementation or fixture: their parity is unpinned beyond the shared statement
-runner.
+checked against them in tests/test_oracle_golden.py. tests/golden/kernels.npz holds the
+outputs of the reference's own TileLang kernels (fa_forward, decode_partial + decode_combine,
+fp8gemm; perfmodel/testset/gen.py) run on a B200 by tests/golden/make_kernel_golden.py; the
+non-causal attention, the split / combine decode and the unscaled FP8 product here match them
+within the kernels' f16 roundings (same test file). The causal mask, the LSE output, the FP8
+block scales and variable decode lengths have no reference kernel: the cases' statements
+define them, and the statement runner fixtures pin the oracle to those.
 """

@@ -111,11 +111,11 @@ def test_gemm_bf16_8192_sampled_rows(cuda_device):
 
 
 # Shapes the default routing sends to the 2-SM pair kernel (256x256 tiles over CTA pairs):
-# pair tiles >= SMs / 2 and no more waves than 128x256 tiles on 148 SMs, e.g. 3000 x 2900:
+# pair tiles >= SMs / 2 and no more waves than 128x256 tiles on 148 SMs, e.g. 3000 x 2904:
 # 12 x 12 = 144 pair tiles (2 waves of 74) against 24 x 12 = 288 one-SM tiles (2 waves of 148).
 # Every one has ragged M and N (not multiples of 256) and most a K tail (not a multiple of 64).
 PAIR_SHAPES = [
-    (3000, 2900, 1000),
+    (3000, 2904, 1000),
     (2304, 4352, 264),
     (4100, 2600, 1032),
     (2200, 2312, 72),
