@@ -11,10 +11,11 @@
 //     different SMs, so that head's K and V come from HBM once and then from L2), heaviest
 //     pair first, in a snake order that balances the causal triangle;
 //   * three warpgroups: warps 0-3 and 4-7 are the softmax warpgroups of tiles A and B
-//     (thread = query row = TMEM lane); in the third, warp 8 is the TMA producer of Q (once
-//     per unit) and K (3-stage ring), warp 9 the TMEM owner and MMA issuer (the warp walks
-//     the schedule, one elected lane issues), warp 10 the TMA producer of V (2-stage ring),
-//     warp 11 idle; all loads go through 4-D
+//     (thread = query row = TMEM lane); in the third, warp 8 is the TMA producer of Q_A and
+//     K (3-stage ring), warp 9 the TMEM owner and MMA issuer (the warp walks the schedule,
+//     one elected lane issues), warp 10 the TMA producer of Q_B and V (2-stage ring), warp 11
+//     idle; each Q tile has its own barriers and is loaded as soon as the unit's last S of
+//     that tile has read the previous one; all loads go through 4-D
 //     maps over [B, S, H, D] with 128-byte swizzle. setmaxnreg moves registers from the
 //     third warpgroup (88 per thread) to the softmax ones (208), which hold a whole S row;
 //   * TMEM: S_A, S_B (128 columns each), O_A, O_B (128 each). P (bf16) is written back over
@@ -24,7 +25,9 @@
 //     S into P the tensor core works for the other; tcgen05 ops of one thread complete in
 //     order, so "S(j) done" also means "PV(j-1) done" for the same tile. The softmax
 //     publishes P in two halves (keys 0-63, 64-127) and PV starts on the first while the
-//     second is computed;
+//     second is computed. A unit's last KV step is tile B's alone; when the next unit's Q_A
+//     and first K tile have landed by then, its S_A(0) is issued before that step's PV_B, so
+//     the tensor core and tile A's softmax work while B's diagonal softmax finishes;
 //   * softmax in one pass over a row held in registers: max on raw scores (3-input max),
 //     packed f32x2 FFMA for scale-and-subtract, and the exponentials split between the MUFU
 //     (ex2.approx.ftz) and the FMA pipe (Cody-Waite reduction 2^x = 2^j 2^f, |f| <= 1/2, with
@@ -36,6 +39,7 @@
 //   * every mbarrier wait is bounded.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "kta_common.cuh"
 #include "kta_host.h"
@@ -81,9 +85,9 @@ struct Layout {
   static constexpr int OFF_K = OFF_Q + 2 * TILE;
   static constexpr int OFF_V = OFF_K + K_STAGES * TILE;
   static constexpr int OFF_BAR = OFF_V + V_STAGES * TILE;
-  // q_full, q_empty, k_full[K], k_empty[K], v_full[V], v_empty[V], s_full[2],
+  // q_full[2], q_empty[2] (per query tile), k_full[K], k_empty[K], v_full[V], v_empty[V], s_full[2],
   // p_full[2][2] (tile, half of P), o_done[2], o_free[2]
-  static constexpr int NUM_BARS = 2 + 2 * K_STAGES + 2 * V_STAGES + 10;
+  static constexpr int NUM_BARS = 4 + 2 * K_STAGES + 2 * V_STAGES + 10;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int TOTAL = OFF_MISC + 16;
   static constexpr int ALLOC = TOTAL + 1024;
@@ -97,6 +101,7 @@ struct Params {
   int q_tiles;         // ceil(S / 128)
   int pairs;           // ceil(q_tiles / 2)
   float scale_log2;    // softmax scale * log2(e)
+  int tail;            // issue the next unit's first S_A during the last (tile B only) step
   unsigned int* status;
 };
 
@@ -107,6 +112,21 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
+}
+
+// Non-blocking probe of an mbarrier phase (mbarrier.test_wait): true once it completed.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n"
+      " .reg .pred P;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, P;\n"
+      "}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
 }
 
 __device__ __forceinline__ bool elect_one_sync() {
@@ -285,9 +305,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Layout::OFF_BAR);
-  uint64_t* q_full = bars;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;
+  uint64_t* q_full = bars;        // [tile]: Q_A (the QK warp loads it), Q_B (the V warp)
+  uint64_t* q_empty = bars + 2;   // [tile]: released by the unit's last S of that tile
+  uint64_t* k_full = bars + 4;
   uint64_t* k_empty = k_full + K_STAGES;
   uint64_t* v_full = k_empty + K_STAGES;
   uint64_t* v_empty = v_full + V_STAGES;
@@ -301,8 +321,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = warp_id();
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&q_full[t], 1);
+      mbar_init(&q_empty[t], 1);
+    }
     for (int s = 0; s < K_STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -347,24 +369,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // ------------------- TMA producers: Q and K (warp 8), V (warp 10) -------------------
       if (lane == 0) {
         const bool is_k = warp == QK_PRODUCER_WARP;
+        // the QK warp loads Q_A and K, the V warp Q_B and V: each Q tile is loaded as soon as
+        // its slot is free, the other tile's slot may still be in use
+        const int qt = is_k ? 0 : 1;
         uint32_t kv_t = 0, qphase = 0;
         bool ok = true;
         for (int k = 0; k < rounds && ok; ++k) {
           const int u = snake(k, blockIdx.x, gridDim.x);
           if (u >= num_units) continue;
           const Unit un = unit_of(u, p);
-          if (is_k) {
-            if (!mbar_wait(q_empty, qphase ^ 1u, abort_flag, p.status, SITE_PROD_Q)) break;
+          if (is_k || un.has_b) {
+            if (!mbar_wait(&q_empty[qt], qphase ^ 1u, abort_flag, p.status, SITE_PROD_Q)) break;
             qphase ^= 1u;
-            const int q0 = 2 * un.pair * BM;
-            mbar_arrive_expect_tx(q_full, un.has_b ? 2 * TILE : TILE);
-            tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q, 0, un.h, q0, un.b);
-            tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + HALF, 64, un.h, q0, un.b);
-            if (un.has_b) {
-              tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE, 0, un.h, q0 + BM, un.b);
-              tma_load_4d(&tmQ, q_full, smem + Layout::OFF_Q + TILE + HALF, 64, un.h, q0 + BM,
-                          un.b);
-            }
+            const int q0 = 2 * un.pair * BM + qt * BM;
+            uint8_t* qdst = smem + Layout::OFF_Q + qt * TILE;
+            mbar_arrive_expect_tx(&q_full[qt], TILE);
+            tma_load_4d(&tmQ, &q_full[qt], qdst, 0, un.h, q0, un.b);
+            tma_load_4d(&tmQ, &q_full[qt], qdst + HALF, 64, un.h, q0, un.b);
           }
           const int nst = is_k ? K_STAGES : V_STAGES;
           uint64_t* fullb = is_k ? k_full : v_full;
@@ -393,10 +414,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc_s = make_idesc(BM, BN, 1u, 1u, 0u, 0u);  // Q K^T, both K-major
       constexpr uint32_t idesc_o = make_idesc(BM, D, 1u, 1u, 0u, 1u);   // P (TMEM) V (MN-major)
       const uint64_t qdesc = sdesc_sw128(smem_u32(smem + Layout::OFF_Q), 16, 1024);
-      uint32_t kv_t = 0, qphase = 0;
+      uint32_t kv_t = 0;
+      uint32_t qphase[2] = {0, 0};
       uint32_t pphase[2] = {0, 0};
       uint32_t ofree_phase[2] = {0, 0};
       int units_done = 0;
+      bool s_a_issued = false;  // the unit's S_A(0) went out during the previous unit's tail
       bool ok = true;
       // descriptor start addresses are in 16-byte units: stepping one adds (bytes >> 4)
       auto issue_s = [&](int tile, uint64_t kdesc, uint64_t* extra0, uint64_t* extra1) {
@@ -455,16 +478,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int u = snake(k, blockIdx.x, gridDim.x);
         if (u >= num_units) continue;
         const Unit un = unit_of(u, p);
-        if (!mbar_wait(q_full, qphase, abort_flag, p.status, SITE_MMA_Q)) break;
-        qphase ^= 1u;
+        if (!s_a_issued) {
+          if (!mbar_wait(&q_full[0], qphase[0], abort_flag, p.status, SITE_MMA_Q)) break;
+          qphase[0] ^= 1u;
+        }
         tc_fence_after();
         const int a_last = 2 * un.pair;  // tile A's diagonal KV tile
         uint64_t prev_vdesc = 0;
         for (int j = 0; j < un.nkv && ok; ++j, ++kv_t) {
           const int ks = static_cast<int>(kv_t % K_STAGES);
           const int vs = static_cast<int>(kv_t % V_STAGES);
-          if (!mbar_wait(&k_full[ks], (kv_t / K_STAGES) & 1u, abort_flag, p.status,
-                         SITE_MMA_K)) {
+          const bool pre = j == 0 && s_a_issued;  // K(0) was waited for in the tail
+          if (!pre && !mbar_wait(&k_full[ks], (kv_t / K_STAGES) & 1u, abort_flag, p.status,
+                                 SITE_MMA_K)) {
             ok = false;
             break;
           }
@@ -473,9 +499,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t vdesc =
               sdesc_sw128(smem_u32(smem + Layout::OFF_V + vs * TILE), HALF, 1024);
           const bool a_on = j <= a_last;
-          // K(j) is released by the commit after its last reader; Q after the unit's last S
-          uint64_t* q_rel = j == un.nkv - 1 ? q_empty : nullptr;
-          if (a_on) issue_s(0, kdesc, un.has_b ? nullptr : &k_empty[ks], un.has_b ? nullptr : q_rel);
+          // K(j) is released by the commit after its last reader; each Q tile after its
+          // tile's last S
+          if (a_on && !pre) {
+            issue_s(0, kdesc, un.has_b ? nullptr : &k_empty[ks],
+                    j == a_last ? &q_empty[0] : nullptr);
+          }
           if (un.has_b && j > 0) {
             // V(j-1) is free once PV_B(j-1) (and everything before it) completed
             if (!issue_pv(1, prev_vdesc, j - 1 == 0, &v_empty[(kv_t - 1) % V_STAGES], nullptr)) {
@@ -483,7 +512,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               break;
             }
           }
-          if (un.has_b) issue_s(1, kdesc, &k_empty[ks], q_rel);
+          if (un.has_b) {
+            if (j == 0) {
+              if (!mbar_wait(&q_full[1], qphase[1], abort_flag, p.status, SITE_MMA_Q)) {
+                ok = false;
+                break;
+              }
+              qphase[1] ^= 1u;
+              tc_fence_after();
+            }
+            issue_s(1, kdesc, &k_empty[ks], j == un.nkv - 1 ? &q_empty[1] : nullptr);
+          }
           if (!mbar_wait(&v_full[vs], (kv_t / V_STAGES) & 1u, abort_flag, p.status,
                          SITE_MMA_V)) {
             ok = false;
@@ -500,6 +539,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           prev_vdesc = vdesc;
         }
         if (!ok) break;
+        // Tail: the last step is tile B's alone, and its PV waits for the softmax of B's
+        // diagonal tile. When the next unit's Q_A and first K tile have landed, its S_A(0)
+        // goes to the tensor core now (after this unit's last PV_A: in order), so that the
+        // tensor core and tile A's softmax work while B's finishes.
+        s_a_issued = false;
+        if (p.tail && un.has_b && k + 1 < rounds) {
+          const int v = snake(k + 1, blockIdx.x, gridDim.x);
+          if (v < num_units) {
+            const Unit nx = unit_of(v, p);
+            const int ks = static_cast<int>(kv_t % K_STAGES);
+            const int ready = (mbar_test(&q_full[0], qphase[0]) &&
+                               mbar_test(&k_full[ks], (kv_t / K_STAGES) & 1u)) ? 1 : 0;
+            if (__shfl_sync(0xffffffffu, ready, 0)) {
+              qphase[0] ^= 1u;
+              tc_fence_after();
+              const uint64_t kdesc =
+                  sdesc_sw128(smem_u32(smem + Layout::OFF_K + ks * TILE), 16, 1024);
+              issue_s(0, kdesc, nx.has_b ? nullptr : &k_empty[ks],
+                      nx.pair == 0 ? &q_empty[0] : nullptr);  // S_A(0) is A's last S then
+              s_a_issued = true;
+            }
+          }
+        }
         if (un.has_b) {
           if (!issue_pv(1, prev_vdesc, un.nkv - 1 == 0, &o_done[1],
                         &v_empty[(kv_t - 1) % V_STAGES])) {
@@ -637,6 +699,9 @@ int launch(const void* Q, const void* K, const void* V, void* O, void* LSE, int6
   prm.q_tiles = static_cast<int>((S + BM - 1) / BM);
   prm.pairs = (prm.q_tiles + 1) / 2;
   prm.scale_log2 = scale * 1.4426950408889634f;
+  // KTA_ATTN_TAIL=0 switches the tail overlap off (comparison runs)
+  prm.tail = 1;
+  if (const char* e = std::getenv("KTA_ATTN_TAIL")) prm.tail = std::atoi(e) != 0;
   prm.status = device_status_ptr();
   s = set_kernel_smem(reinterpret_cast<const void*>(attn_fwd_kernel), Layout::ALLOC);
   if (s != KTA_OK) return s;
