@@ -374,10 +374,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int qt = is_k ? 0 : 1;
         uint32_t kv_t = 0, qphase = 0;
         bool ok = true;
+        // Per unit: the first K (or V) tile, then the Q tile (its slot frees only at the
+        // previous unit's last S of that tile), then the remaining tiles, so that the first
+        // K / V tile of a unit does not queue behind the wait for the Q slot.
+        auto load_kv = [&](const Unit& un, int j) -> bool {
+          const int nst = is_k ? K_STAGES : V_STAGES;
+          uint64_t* fullb = is_k ? k_full : v_full;
+          uint64_t* emptyb = is_k ? k_empty : v_empty;
+          const CUtensorMap* map = is_k ? &tmK : &tmV;
+          uint8_t* base = smem + (is_k ? Layout::OFF_K : Layout::OFF_V);
+          const int st = static_cast<int>(kv_t % nst);
+          const uint32_t ph = (kv_t / nst) & 1u;
+          if (!mbar_wait(&emptyb[st], ph ^ 1u, abort_flag, p.status, SITE_PROD_KV)) return false;
+          uint8_t* dst = base + st * TILE;
+          mbar_arrive_expect_tx(&fullb[st], TILE);
+          tma_load_4d(map, &fullb[st], dst, 0, un.h, j * BN, un.b);
+          tma_load_4d(map, &fullb[st], dst + HALF, 64, un.h, j * BN, un.b);
+          ++kv_t;
+          return true;
+        };
         for (int k = 0; k < rounds && ok; ++k) {
           const int u = snake(k, blockIdx.x, gridDim.x);
           if (u >= num_units) continue;
           const Unit un = unit_of(u, p);
+          if (!load_kv(un, 0)) break;
           if (is_k || un.has_b) {
             if (!mbar_wait(&q_empty[qt], qphase ^ 1u, abort_flag, p.status, SITE_PROD_Q)) break;
             qphase ^= 1u;
@@ -387,23 +407,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tma_load_4d(&tmQ, &q_full[qt], qdst, 0, un.h, q0, un.b);
             tma_load_4d(&tmQ, &q_full[qt], qdst + HALF, 64, un.h, q0, un.b);
           }
-          const int nst = is_k ? K_STAGES : V_STAGES;
-          uint64_t* fullb = is_k ? k_full : v_full;
-          uint64_t* emptyb = is_k ? k_empty : v_empty;
-          const CUtensorMap* map = is_k ? &tmK : &tmV;
-          uint8_t* base = smem + (is_k ? Layout::OFF_K : Layout::OFF_V);
-          for (int j = 0; j < un.nkv; ++j, ++kv_t) {
-            const int st = static_cast<int>(kv_t % nst);
-            const uint32_t ph = (kv_t / nst) & 1u;
-            if (!mbar_wait(&emptyb[st], ph ^ 1u, abort_flag, p.status, SITE_PROD_KV)) {
-              ok = false;
-              break;
-            }
-            uint8_t* dst = base + st * TILE;
-            mbar_arrive_expect_tx(&fullb[st], TILE);
-            tma_load_4d(map, &fullb[st], dst, 0, un.h, j * BN, un.b);
-            tma_load_4d(map, &fullb[st], dst + HALF, 64, un.h, j * BN, un.b);
-          }
+          for (int j = 1; j < un.nkv && ok; ++j) ok = load_kv(un, j);
         }
       }
     } else if (warp == MMA_WARP) {
