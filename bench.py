@@ -655,6 +655,14 @@ class Fp8Workload:
     graph_default = False
     peak_key = "fp8"
 
+    def kernels_per_step(self) -> int:
+        """The main launch, plus the quarter launch when the tiles of a ragged last round are
+        cut into quarters (the rule of kta_gemm_fp8_blockscaled)."""
+        tiles = -(-self.m // 128) * -(-self.n // 256)
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        rem = tiles % sms if tiles > sms else 0
+        return 2 if rem > 0 and rem * 4 <= sms and os.environ.get("KTA_FP8_SPLIT") != "0" else 1
+
     def __init__(self, dist: Dist, m: int = 4096, n: int = 7168, k: int = 7168) -> None:
         self.m, self.n_total, self.k = m, n, k
         lo, hi = shard(n, dist.world, dist.rank, align=128)
@@ -1202,6 +1210,12 @@ def time_e2e(wl, steps: int, dist: Dist, device: torch.device) -> dict:
     return {"total_ms": e0.elapsed_time(e1), "pipelines": 2}
 
 
+def wl_kernels_per_step(wl) -> int:
+    """Kernels of this library one step launches: 1, or the workload's own count."""
+    fn = getattr(wl, "kernels_per_step", None)
+    return int(fn()) if callable(fn) else 1
+
+
 def gather_outputs(wl, dist: Dist, reps: int = 5) -> dict | None:
     """The optional all-gather of every rank's output block over NCCL (torch.distributed,
     NVLink), timed on its own after the timed region: `reps` all-gathers of the workload's
@@ -1423,7 +1437,7 @@ def run_kta(args, dist: Dist) -> dict | None:
                     "pipelines": e2e.get("pipelines", 1)},
             "cpu_baseline": cpu,
             "clocks": ck,
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * wl_kernels_per_step(wl),
             "graph_b2b": graph_b2b,
             "protocol": protocol,
             "allgather": gathered,

@@ -21,6 +21,7 @@
 //   * every mbarrier wait is bounded.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "kta_common.cuh"
 #include "kta_host.h"
@@ -63,8 +64,16 @@ struct Params {
   const float* sb;     // [NB, KB]
   __nv_bfloat16* c;    // [M, N]
   int M, N, K, KB, NB;
+  int items;           // work items of this launch (tiles, or quarters of tiles)
+  int tile_base;       // the quarter launch: raster index of the first tile it cuts up
   unsigned int* status;
 };
+
+// The quarter launch: tiles that would fill only part of the last round of the main launch
+// are cut into 128 x 64 quarters and run by a second launch on the SMs the main one has left
+// idle, so that the round takes about a quarter of the time.
+constexpr int SUB = 4;
+constexpr int SUB_N = BN / SUB;
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb,
                                             int& nb) {
@@ -77,6 +86,9 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = r / gsz;
 }
 
+// QTR: items are 128 x 64 quarters of the tiles from p.tile_base on (B through a map with a
+// 64-row box; each promotion warp holds 16 of the quarter's columns); otherwise whole tiles.
+template <bool QTR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const Params p) {
@@ -119,27 +131,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
   const int tiles_m = (p.M + BM - 1) / BM;
   const int tiles_n = (p.N + BN - 1) / BN;
-  const int num_tiles = tiles_m * tiles_n;
+  const int num_tiles = p.items;
   const int KB = p.KB;
+  // tile (mb, nb) of item `it`, and the first accumulator / output column of the item
+  auto coords = [&](int it, int& mb, int& nb, int& col) {
+    if constexpr (QTR) {
+      tile_coords(p.tile_base + it / SUB, tiles_m, tiles_n, mb, nb);
+      col = (it % SUB) * SUB_N;
+    } else {
+      tile_coords(it, tiles_m, tiles_n, mb, nb);
+      col = 0;
+    }
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      constexpr int b_bytes = QTR ? Layout::B_BYTES / SUB : Layout::B_BYTES;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        int mb, nb;
-        tile_coords(tile, tiles_m, tiles_n, mb, nb);
+        int mb, nb, col;
+        coords(tile, mb, nb, col);
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PROD)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], Layout::A_BYTES + Layout::B_BYTES);
+          mbar_arrive_expect_tx(&full[stage], Layout::A_BYTES + b_bytes);
           tma_load_2d(&tmA, &full[stage], smem + Layout::OFF_A + stage * Layout::A_BYTES,
                       kb * BK, mb * BM);
           tma_load_2d(&tmB, &full[stage], smem + Layout::OFF_B + stage * Layout::B_BYTES,
-                      kb * BK, nb * BN);
+                      kb * BK, nb * BN + col);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -149,7 +172,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(BM, BN, 0u, 0u, 0u, 0u);  // e4m3 x e4m3 -> f32
+      // e4m3 x e4m3 -> f32
+      constexpr uint32_t idesc = make_idesc(BM, QTR ? SUB_N : BN, 0u, 0u, 0u, 0u);
       int stage = 0;
       uint32_t phase = 0;
       int buf = 0;
@@ -191,18 +215,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int buf = 0;
     uint32_t bphase = 0;
     bool ok = true;
+    // columns of the accumulator this warp promotes (a quarter: 16 of its 64)
+    constexpr int COLS = QTR ? SUB_N / 4 : PROMO_COLS;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      int mb, nb;
-      tile_coords(tile, tiles_m, tiles_n, mb, nb);
+      int mb, nb, col;
+      coords(tile, mb, nb, col);
       const int m = mb * BM + row;
-      const int nblk = nb * 2 + half;  // weight-scale block of this warp's columns
+      const int c0 = QTR ? cg * COLS : cg * PROMO_COLS;  // first accumulator column
+      const int nblk = QTR ? (nb * BN + col) / 128 : nb * 2 + half;  // weight-scale block
       const bool row_in = m < p.M;
       const bool blk_in = nblk < p.NB;
       const float* sa_row = p.sa + static_cast<long long>(row_in ? m : 0) * KB;
       const float* sb_row = p.sb + static_cast<long long>(blk_in ? nblk : 0) * KB;
-      uint64_t acc[PROMO_COLS / 2];  // packed pairs of fp32 accumulators
+      uint64_t acc[COLS / 2];  // packed pairs of fp32 accumulators
 #pragma unroll
-      for (int i = 0; i < PROMO_COLS / 2; ++i) acc[i] = 0ull;
+      for (int i = 0; i < COLS / 2; ++i) acc[i] = 0ull;
       float scale_next = (row_in && blk_in) ? __ldg(sa_row) * __ldg(sb_row) : 0.f;
       for (int kb = 0; kb < KB; ++kb) {
         const float scale = scale_next;
@@ -214,10 +241,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t t = tmem + lane_base + buf * BN + cg * PROMO_COLS;
+        const uint32_t t = tmem + lane_base + buf * BN + c0;
         const uint64_t s2 = f2(scale, scale);
 #pragma unroll
-        for (int c = 0; c < PROMO_COLS; c += 16) {
+        for (int c = 0; c < COLS; c += 16) {
           uint32_t r[16];
           tmem_ld_32x32b_x16(t + c, r);
           tmem_ld_wait();
@@ -235,18 +262,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (buf == 0) bphase ^= 1u;
       }
       if (!ok) break;
-      const int n0 = nb * BN + cg * PROMO_COLS;
+      const int n0 = nb * BN + col + c0;
       if (row_in && n0 < p.N) {
         __nv_bfloat16* crow = p.c + static_cast<long long>(m) * p.N + n0;
-        uint32_t pk[PROMO_COLS / 2];
+        uint32_t pk[COLS / 2];
 #pragma unroll
-        for (int i = 0; i < PROMO_COLS / 2; ++i) {
+        for (int i = 0; i < COLS / 2; ++i) {
           float x0, x1;
           f2_split(acc[i], x0, x1);
           pk[i] = pack_bf16x2(x0, x1);
         }
 #pragma unroll
-        for (int c = 0; c < PROMO_COLS; c += 8) {
+        for (int c = 0; c < COLS; c += 8) {
           if (n0 + c < p.N) {
             *reinterpret_cast<uint4*>(crow + c) =
                 make_uint4(pk[c / 2], pk[c / 2 + 1], pk[c / 2 + 2], pk[c / 2 + 3]);
@@ -286,11 +313,12 @@ int launch(const void* A, const void* sa, const void* B, const void* sb, void* C
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != KTA_OK) return s;
   }
-  {
+  CUtensorMap tbq;  // B with a 64-row box, for the quarter launch
+  for (int i = 0; i < 2; ++i) {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
     const uint64_t strides[1] = {static_cast<uint64_t>(K)};
-    const uint32_t box[2] = {BK, BN};
-    s = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, B, dims, strides, box,
+    const uint32_t box[2] = {BK, static_cast<uint32_t>(i == 0 ? BN : SUB_N)};
+    s = encode_tmap(i == 0 ? &tb : &tbq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, B, dims, strides, box,
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != KTA_OK) return s;
   }
@@ -304,12 +332,28 @@ int launch(const void* A, const void* sa, const void* B, const void* sb, void* C
   prm.KB = (K + BK - 1) / BK;
   prm.NB = (N + 127) / 128;
   prm.status = device_status_ptr();
-  s = set_kernel_smem(reinterpret_cast<const void*>(fp8_gemm_kernel), Layout::ALLOC);
-  if (s != KTA_OK) return s;
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = std::max(1, std::min(tiles, current_sm_count()));
-  return launch_ex(fp8_gemm_kernel, dim3(grid), dim3(NUM_THREADS), Layout::ALLOC, stream, 1, ta,
-                   tb, prm);
+  const int sms = std::max(1, current_sm_count());
+  // The tiles of a ragged last round (4096 x 7168: 896 tiles = 6 rounds of 148 + 8) go to a
+  // second launch as quarters when those fit in one round on the SMs (8 -> 32 quarters);
+  // KTA_FP8_SPLIT=0 keeps them whole (comparison runs).
+  const int rem = tiles > sms ? tiles % sms : 0;
+  const char* split = std::getenv("KTA_FP8_SPLIT");
+  const bool quarters = rem > 0 && rem * SUB <= sms && (split == nullptr || split[0] != '0');
+  const int main_tiles = quarters ? tiles - rem : tiles;
+  s = set_kernel_smem(reinterpret_cast<const void*>(fp8_gemm_kernel<false>), Layout::ALLOC);
+  if (s != KTA_OK) return s;
+  prm.items = main_tiles;
+  prm.tile_base = 0;
+  s = launch_ex(fp8_gemm_kernel<false>, dim3(std::min(main_tiles, sms)), dim3(NUM_THREADS),
+                Layout::ALLOC, stream, 1, ta, tb, prm);
+  if (s != KTA_OK || !quarters) return s;
+  s = set_kernel_smem(reinterpret_cast<const void*>(fp8_gemm_kernel<true>), Layout::ALLOC);
+  if (s != KTA_OK) return s;
+  prm.items = rem * SUB;
+  prm.tile_base = main_tiles;
+  return launch_ex(fp8_gemm_kernel<true>, dim3(rem * SUB), dim3(NUM_THREADS), Layout::ALLOC,
+                   stream, 1, ta, tbq, prm);
 }
 
 }  // namespace fp8

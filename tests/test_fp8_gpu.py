@@ -42,10 +42,12 @@ def _check(y, ref):
     assert np.linalg.norm(y - ref) <= 2e-2 * np.linalg.norm(ref)
 
 
-# 18944 x 256: 148 tiles of 128 x 256, exactly one per SM of a B200.
+# 18944 x 256: 148 tiles of 128 x 256, exactly one per SM of a B200. 19072 x 256: 149 tiles,
+# the last cut into four 128 x 64 quarters; 19200 x 264: 300 tiles, the 4 of the last round
+# cut into quarters, three of each lying wholly past N = 264 (they write nothing).
 @pytest.mark.parametrize("m,n,k", [(128, 256, 128), (256, 512, 1024), (300, 520, 208),
                                    (1, 256, 128), (130, 136, 4096), (512, 1024, 7168),
-                                   (18944, 256, 256)])
+                                   (18944, 256, 256), (19072, 256, 256), (19200, 264, 384)])
 def test_fp8_blockscaled(cuda_device, m, n, k):
     ac, sa, bc, sb = _make(m, n, k)
     y = _run(cuda_device, ac, sa, bc, sb)
@@ -57,10 +59,22 @@ def test_fp8_blockscaled_baseline_config_sampled_rows(cuda_device):
     m, n, k = 4096, 7168, 7168
     ac, sa, bc, sb = _make(m, n, k, seed=1)
     y = _run(cuda_device, ac, sa, bc, sb)
+    # rows 3072 .. 4095 hold the 8 tiles of the last round (cut into quarters), columns
+    # 6912 .. 7167
     rows = np.concatenate([np.random.default_rng(2).choice(m, 60, replace=False),
-                           [0, 127, 128, m - 1]])
+                           [0, 127, 128, 3072, 3500, 3583, 3584, m - 1]])
     ref = ofp8.dequant_rows(ac[rows], sa[rows]) @ ofp8.dequant_blocks(bc, sb).T
     _check(y[rows], ref)
+
+
+def test_fp8_quarters_match_whole_tiles(cuda_device, monkeypatch):
+    """The tail quarters give the same bits as the same tiles computed whole
+    (KTA_FP8_SPLIT=0): the same products and the same fp32 promotion order."""
+    ac, sa, bc, sb = _make(19072, 512, 512, seed=4)
+    y1 = _run(cuda_device, ac, sa, bc, sb)
+    monkeypatch.setenv("KTA_FP8_SPLIT", "0")
+    y2 = _run(cuda_device, ac, sa, bc, sb)
+    np.testing.assert_array_equal(y1, y2)
 
 
 def test_fp8_uses_the_scales(cuda_device):
