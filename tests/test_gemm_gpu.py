@@ -178,6 +178,32 @@ def test_gemm_8192_with_k_tail_sampled_rows(cuda_device, monkeypatch, route):
     assert not torch.isnan(c.float()).any()
 
 
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+@pytest.mark.parametrize("m,n,k", [(1000, 1032, 264), (3000, 2904, 1000), (16, 4096, 1024),
+                                   (40, 2048, 512)])
+def test_gemm_padded_leading_dimensions(cuda_device, m, n, k, layout):
+    """A, B and C as views into wider row-major buffers (lda, ldb, ldc larger than the logical
+    row, all multiples of 8): every path reads and writes through the leading dimensions, and
+    the padding columns of C stay untouched."""
+    from kta_b200 import ops
+
+    pad = 24
+    a, b = _inputs(m, n, k, torch.bfloat16, seed=9, b_layout=layout)
+    abuf = torch.zeros(m, k + pad, dtype=torch.bfloat16, device=cuda_device)
+    abuf[:, :k] = a.to(cuda_device)
+    rows_b, cols_b = b.shape
+    bbuf = torch.zeros(rows_b, cols_b + pad, dtype=torch.bfloat16, device=cuda_device)
+    bbuf[:, :cols_b] = b.to(cuda_device)
+    cbuf = torch.full((m, n + pad), 7.0, dtype=torch.bfloat16, device=cuda_device)
+    c = cbuf[:, :n]
+    ops.gemm(abuf[:, :k], bbuf[:, :cols_b], out=c, b_layout=layout)
+    torch.cuda.synchronize()
+    ref = (ogemm.gemm_tn if layout == "nk" else ogemm.gemm_nn)(a.double().numpy(),
+                                                               b.double().numpy())
+    _check(c, ref)
+    assert torch.all(cbuf[:, n:] == 7.0)
+
+
 def test_gemm_is_deterministic(cuda_device):
     from kta_b200 import ops
 
