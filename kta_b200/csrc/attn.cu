@@ -51,7 +51,7 @@ constexpr int D = 128;
 constexpr int BM = 128;                 // query rows per tile
 constexpr int BN = 128;                 // KV rows per tile
 constexpr int NUM_THREADS = 384;        // two softmax warpgroups, producers + MMA warpgroup
-constexpr int K_STAGES = 3;
+constexpr int K_STAGES = 2;
 constexpr int V_STAGES = 2;
 constexpr int QK_PRODUCER_WARP = 8;
 constexpr int MMA_WARP = 9;
