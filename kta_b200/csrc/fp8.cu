@@ -225,16 +225,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int nblk = QTR ? (nb * BN + col) / 128 : nb * 2 + half;  // weight-scale block
       const bool row_in = m < p.M;
       const bool blk_in = nblk < p.NB;
-      const float* sa_row = p.sa + static_cast<long long>(row_in ? m : 0) * KB;
-      const float* sb_row = p.sb + static_cast<long long>(blk_in ? nblk : 0) * KB;
+      // 32-bit offsets into the scale arrays (the launch checks M x KB and NB x KB < 2^31);
+      // the bases stay kernel parameters. The scales of K block kb+2 are loaded while block
+      // kb is folded and multiplied only when used, so no load latency lands on the
+      // promotion path.
+      const bool live = row_in && blk_in;
+      const int sa_off = live ? m * KB : 0;
+      const int sb_off = live ? nblk * KB : 0;
       uint64_t acc[COLS / 2];  // packed pairs of fp32 accumulators
 #pragma unroll
       for (int i = 0; i < COLS / 2; ++i) acc[i] = 0ull;
-      float scale_next = (row_in && blk_in) ? __ldg(sa_row) * __ldg(sb_row) : 0.f;
+      float a0 = 0.f, b0 = 0.f, a1 = 0.f, b1 = 0.f;  // scales of blocks kb and kb+1
+      if (live) {
+        a0 = __ldg(p.sa + sa_off);
+        b0 = __ldg(p.sb + sb_off);
+        if (KB > 1) {
+          a1 = __ldg(p.sa + sa_off + 1);
+          b1 = __ldg(p.sb + sb_off + 1);
+        }
+      }
       for (int kb = 0; kb < KB; ++kb) {
-        const float scale = scale_next;
-        if (kb + 1 < KB) {
-          scale_next = (row_in && blk_in) ? __ldg(sa_row + kb + 1) * __ldg(sb_row + kb + 1) : 0.f;
+        const float scale = a0 * b0;
+        a0 = a1;
+        b0 = b1;
+        if (live && kb + 2 < KB) {
+          a1 = __ldg(p.sa + sa_off + kb + 2);
+          b1 = __ldg(p.sb + sb_off + kb + 2);
         }
         if (!mbar_wait(&tfull[buf], bphase, abort_flag, p.status, SITE_PROMO)) {
           ok = false;
@@ -296,6 +312,11 @@ int launch(const void* A, const void* sa, const void* B, const void* sb, void* C
   if (!A || !sa || !B || !sb || !C) return KTA_ERR_INVALID_ARG;
   if (M64 <= 0 || N64 <= 0 || K64 <= 0) return KTA_ERR_INVALID_ARG;
   if (M64 > (1 << 30) || N64 > (1 << 30) || K64 > (1 << 30)) return KTA_ERR_UNSUPPORTED;
+  // scale arrays indexed with 32-bit offsets (an A or B this large would exceed 256 GB)
+  if (M64 * ((K64 + BK - 1) / BK) >= (int64_t{1} << 31) ||
+      ((N64 + 127) / 128) * ((K64 + BK - 1) / BK) >= (int64_t{1} << 31)) {
+    return KTA_ERR_UNSUPPORTED;
+  }
   if (K64 % 16 != 0 || N64 % 8 != 0) return KTA_ERR_ALIGN;
   if (!aligned16(A) || !aligned16(B) || !aligned16(C) ||
       (reinterpret_cast<uintptr_t>(sa) & 3) || (reinterpret_cast<uintptr_t>(sb) & 3)) {

@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (c == P_BN / EPI_COLS - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(tempty0[acc]);
+          if (lane == 0) mbar_arrive_remote(tempty0[acc]);
         }
         uint32_t pk[32];
 #pragma unroll

@@ -524,9 +524,14 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
       : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
-               : "memory");
+// Arrives on a barrier of either CTA of the pair (`bar_cluster` is a shared::cluster
+// address) with release at CTA scope. For "this thread's TMEM reads are over" (its
+// tcgen05.wait::ld has returned and tcgen05.fence::before_thread_sync precedes the arrival)
+// nothing needs publishing at cluster scope; a release.cluster arrival instead costs a fence
+// of about 1400 cycles per call (clock64 timeline of a pair kernel that arrived once per
+// K block).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
 }  // namespace kta
