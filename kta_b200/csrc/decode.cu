@@ -304,28 +304,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int pair = sg.b * p.hkv + sg.kvh;
       // Slot of a partial segment: the CTA's first segment uses 2c, its last 2c + 1.
       const int slot = 2 * static_cast<int>(blockIdx.x) + (t == my_begin ? 0 : 1);
-      for (int idx = lane; idx < G * D; idx += 32) {
-        const int g = idx / D, d = idx - g * D;
+      // Lane g < G folds head g's eight (m, l) states into one normalised weight per warp,
+      // written over that warp's m (only lane g touches head g's entries), and keeps the
+      // head's log2-sum-exp; every output element is then a weighted sum of eight values.
+      float lse_g = -INFINITY;
+      for (int g = lane; g < G; g += 32) {
         float M = -INFINITY;
 #pragma unroll
         for (int wi = 0; wi < COMPUTE_WARPS; ++wi) M = fmaxf(M, merge_ml[(wi * G + g) * 2]);
-        float Lsum = 0.f, acc = 0.f;
-        if (M != -INFINITY) {
+        float fw[COMPUTE_WARPS];
+        float Lsum = 0.f;
 #pragma unroll
-          for (int wi = 0; wi < COMPUTE_WARPS; ++wi) {
-            const float mw = merge_ml[(wi * G + g) * 2];
-            const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-            Lsum += merge_ml[(wi * G + g) * 2 + 1] * f;
-            acc += merge_o[(wi * G + g) * D + d] * f;
-          }
+        for (int wi = 0; wi < COMPUTE_WARPS; ++wi) {
+          const float mw = merge_ml[(wi * G + g) * 2];
+          fw[wi] = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+          Lsum += merge_ml[(wi * G + g) * 2 + 1] * fw[wi];
         }
-        const float val = Lsum > 0.f ? acc / Lsum : 0.f;
+        const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+#pragma unroll
+        for (int wi = 0; wi < COMPUTE_WARPS; ++wi) merge_ml[(wi * G + g) * 2] = fw[wi] * inv;
+        lse_g = Lsum > 0.f ? M + __log2f(Lsum) : -INFINITY;
+      }
+      __syncwarp();
+      for (int idx = lane; idx < G * D; idx += 32) {
+        const int g = idx / D, d = idx - g * D;  // g is the same for the 32 lanes (D = 128)
+        float val = 0.f;
+#pragma unroll
+        for (int wi = 0; wi < COMPUTE_WARPS; ++wi) {
+          val += merge_o[(wi * G + g) * D + d] * merge_ml[(wi * G + g) * 2];
+        }
+        const float lse = __shfl_sync(0xffffffffu, lse_g, g);
         if (!partial) {
           p.out[(static_cast<long long>(sg.b) * p.hq + sg.kvh * G + g) * D + d] =
               __float2bfloat16_rn(val);
         } else {
           p.part_o[(static_cast<long long>(slot) * G + g) * D + d] = val;
-          if (d == 0) p.part_lse[slot * G + g] = Lsum > 0.f ? M + __log2f(Lsum) : -INFINITY;
+          if (d == 0) p.part_lse[slot * G + g] = lse;
         }
       }
       __syncwarp();
@@ -347,7 +361,54 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (last) __threadfence();
         }
         last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
+        constexpr int NC = 4;  // contributors combined with independent loads (the common case)
+        if (last && c_last - c_first < NC) {
+          // Up to four CTAs hold pieces of this pair: per head, every lane issues all their
+          // LSE and output loads at once (one L2 round trip per head instead of one per
+          // contributor and element).
+          int sl[NC];
+          bool on[NC];
+#pragma unroll
+          for (int j = 0; j < NC; ++j) {
+            const int c = c_first + j;
+            on[j] = c <= c_last && w.busy(c);
+            sl[j] = on[j] ? 2 * c + (w.start(c) >= sg.pair_start ? 0 : 1) : 0;
+          }
+          for (int g = 0; g < G; ++g) {
+            float lse[NC], ov[NC][D / 32];
+#pragma unroll
+            for (int j = 0; j < NC; ++j) {
+              lse[j] = on[j] ? __ldcg(p.part_lse + sl[j] * G + g) : -INFINITY;
+#pragma unroll
+              for (int u = 0; u < D / 32; ++u) {
+                ov[j][u] = on[j] ? __ldcg(p.part_o + (static_cast<long long>(sl[j]) * G + g) * D +
+                                          u * 32 + lane)
+                                 : 0.f;
+              }
+            }
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < NC; ++j) mx = fmaxf(mx, lse[j]);
+            float wsum = 0.f, acc[D / 32];
+#pragma unroll
+            for (int u = 0; u < D / 32; ++u) acc[u] = 0.f;
+            if (mx != -INFINITY) {
+#pragma unroll
+              for (int j = 0; j < NC; ++j) {
+                const float wt = (lse[j] == -INFINITY) ? 0.f : exp2f(lse[j] - mx);
+                wsum += wt;
+#pragma unroll
+                for (int u = 0; u < D / 32; ++u) acc[u] += wt * ov[j][u];
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < D / 32; ++u) {
+              p.out[(static_cast<long long>(sg.b) * p.hq + sg.kvh * G + g) * D + u * 32 + lane] =
+                  __float2bfloat16_rn(wsum > 0.f ? acc[u] / wsum : 0.f);
+            }
+          }
+          if (lane == 0) p.counters[pair] = 0u;  // ready for the next call
+        } else if (last) {
           for (int idx = lane; idx < G * D; idx += 32) {
             const int g = idx / D, d = idx - g * D;
             float mx = -INFINITY;
