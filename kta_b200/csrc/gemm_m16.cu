@@ -127,6 +127,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   __syncthreads();
   pdl_launch_dependents();
+  if (warp == 0 && lane == 0) {
+    // While the previous grid finishes, pull the boxes of the first ring's worth of stages
+    // into L2, so the stream does not start with a full HBM round trip after the wait.
+    const int pre = num_stages < L::STAGES ? num_stages : L::STAGES;
+    for (int ks = 0; ks < pre; ++ks) {
+#pragma unroll
+      for (int u = 0; u < SUB; ++u) {
+        tma_prefetch_l2_2d(&tmB, ks * STAGE_K + u * BOX_K, row0);
+        if (blockIdx.x == 0) tma_prefetch_l2_2d(&tmA, ks * STAGE_K + u * BOX_K, 0);
+      }
+    }
+  }
   pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
 
   if (warp == 0) {
