@@ -66,6 +66,7 @@ struct Params {
   int M, N, K, KB, NB;
   int items;           // work items of this launch (tiles, or quarters of tiles)
   int tile_base;       // the quarter launch: raster index of the first tile it cuts up
+  int prefetch;        // A and B exceed kPrefetchMinBytes: L2 prefetch before the wait
   unsigned int* status;
 };
 
@@ -127,8 +128,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  pdl_launch_dependents();
-  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
   const int tiles_m = (p.M + BM - 1) / BM;
   const int tiles_n = (p.N + BN - 1) / BN;
   const int num_tiles = p.items;
@@ -143,6 +142,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       col = 0;
     }
   };
+  pdl_launch_dependents();
+  if (p.prefetch && warp == 0 && lane == 0 && static_cast<int>(blockIdx.x) < num_tiles) {
+    // While the previous grid finishes, pull the first ring's K blocks of this CTA's first
+    // item into L2 (a prefetch writes nothing, so it may precede the wait).
+    int mb, nb, col;
+    coords(blockIdx.x, mb, nb, col);
+    for (int kb = 0; kb < KB && kb < STAGES; ++kb) {
+      tma_prefetch_l2_2d(&tmA, kb * BK, mb * BM);
+      tma_prefetch_l2_2d(&tmB, kb * BK, nb * BN + col);
+    }
+  }
+  pdl_wait();  // the previous grid's writes (this launch's inputs) are visible from here on
 
   if (warp == 0) {
     if (lane == 0) {
@@ -352,6 +363,7 @@ int launch(const void* A, const void* sa, const void* B, const void* sb, void* C
   prm.K = K;
   prm.KB = (K + BK - 1) / BK;
   prm.NB = (N + 127) / 128;
+  prm.prefetch = (M64 + N64) * K64 > kPrefetchMinBytes ? 1 : 0;
   prm.status = device_status_ptr();
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int sms = std::max(1, current_sm_count());

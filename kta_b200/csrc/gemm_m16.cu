@@ -98,7 +98,7 @@ __device__ __forceinline__ void compute_bar() {
 template <int NT, bool BF16>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_m16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    void* __restrict__ Cv, int M, int N, int K, int64_t ldc,
+                    void* __restrict__ Cv, int M, int N, int K, int64_t ldc, int prefetch,
                     unsigned int* status) {
   using L = Layout<NT>;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   __syncthreads();
   pdl_launch_dependents();
-  if (warp == 0 && lane == 0) {
+  if (prefetch && warp == 0 && lane == 0) {
     // While the previous grid finishes, pull the boxes of the first ring's worth of stages
     // into L2, so the stream does not start with a full HBM round trip after the wait.
     const int pre = num_stages < L::STAGES ? num_stages : L::STAGES;
@@ -274,8 +274,9 @@ int launch_nt(const void* A, const void* B, void* C, int M, int N, int K, int64_
   if (s != KTA_OK) return s;
   const int tiles8 = (N + 7) / 8;
   const int grid = (tiles8 + NT - 1) / NT;
+  const int prefetch = static_cast<int64_t>(N) * K * 2 > kPrefetchMinBytes ? 1 : 0;
   return launch_ex(kernel, dim3(grid), dim3(THREADS), L::ALLOC, stream, 1, ta, tb, C, M, N, K,
-                   ldc, device_status_ptr());
+                   ldc, prefetch, device_status_ptr());
 }
 
 }  // namespace m16

@@ -42,6 +42,13 @@ int set_kernel_smem(const void* kernel, int bytes);
 // Status of the last kta_so_* call on this host thread (kta_last_error).
 void set_last_error(int s);
 
+// Operand bytes above which a kernel prefetches its first ring of tiles into L2 before
+// griddepcontrol.wait: such operands cannot already sit in the 126 MB L2, so the prefetch
+// overlaps the first HBM round trip with the previous grid's tail. Below it the operands may
+// be L2-resident, and the prefetches only occupy the L2 while the real loads queue behind
+// them (an f16 1024^3 GEMM ran 30 % slower with them).
+constexpr int64_t kPrefetchMinBytes = int64_t{64} << 20;
+
 // Launches `kernel` with programmatic stream serialisation: the next kernel in the stream (or
 // graph) may be scheduled and run its set-up while this one finishes; its griddepcontrol.wait
 // holds every memory access until this grid has completed and its writes are visible.
