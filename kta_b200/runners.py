@@ -90,8 +90,8 @@ _TORCH = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32,
 def resolve(entry: str) -> Callable[..., dict[str, torch.Tensor]]:
     """The runner of ``entry``: a libkta_b200 entry name from RUNNERS, or a plug-in runner
     named ``"package.module:function"`` with the same ``(inputs, shape, outputs) -> outputs``
-    signature, imported on first use (so the checker can judge a caller's own launch code the
-    way the reference's checker judges any built module)."""
+    signature, imported on first use (so the checker can check a caller's own launch code the
+    way the reference's checker checks any built module)."""
     if entry in RUNNERS:
         return RUNNERS[entry]
     if ":" in entry:

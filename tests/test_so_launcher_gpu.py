@@ -74,7 +74,7 @@ def test_so_gemm(cuda_device, entry, dtype, layout, m, n, k):
 def test_so_gemm_nn_f16_on_the_reference_seed_case(cuda_device):
     """The reference's seed case gemm_fp16 (C = A @ B, f16, B [K, N]) at its third shape
     (M = N = 1024, K = 16384), inputs from the reference's `normal` generator (N(0, 1)
-    unscaled, kta_b200.inputs mirrors it), judged with the case's fixed rtol = atol = 1e-2
+    unscaled, kta_b200.inputs mirrors it), checked with the case's fixed rtol = atol = 1e-2
     relative to the output magnitude (|C| ~ sqrt(K) = 128 here)."""
     from kta_b200 import inputs as kinp
 
