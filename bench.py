@@ -770,7 +770,7 @@ class MoeWorkload:
     shape E=8 T=2048 N=1024 K=2048, f16: T / E tokens per expert, W [E, K, N]; this rank's
     expert shard (experts are independent)."""
 
-    kernel_regex = "gemm_kernel"
+    kernel_regex = "gemm"
     unit = "TFLOP/s"
     dtype_name = "f16"
     case = "moe_gemm_f16"

@@ -301,31 +301,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // Per SM the tensor core reads 8 KB of operands per 256x256x16 step instead of 12 KB
 // for the 1-SM 128x256 tile, and L2 serves a third less operand traffic per FLOP.
 // ---------------------------------------------------------------------------------------
-constexpr int P_STAGES = 6;
 constexpr int P_BM = 256;   // rows of A per CTA pair (128 per CTA)
-constexpr int P_BN = 256;   // rows of B per CTA pair (128 per CTA)
 
+// PBN columns per pair tile (256, or 128 for the grouped expert GEMM): PBN / 2 of B per CTA.
+template <int PBN>
 struct PairLayout {
+  static constexpr int STAGES = PBN == 256 ? 6 : 8;
   static constexpr int A_BYTES = 128 * BK * 2;
-  static constexpr int B_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = (PBN / 2) * BK * 2;
   static constexpr int C_BYTES = 32 * EPI_COLS * 2;
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = OFF_A + P_STAGES * A_BYTES;
-  static constexpr int OFF_C = OFF_B + P_STAGES * B_BYTES;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_C = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_BAR = OFF_C + EPI_WARPS * 2 * C_BYTES;
-  static constexpr int NUM_BARS = 2 * P_STAGES + 4;
+  static constexpr int NUM_BARS = 2 * STAGES + 4;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int TOTAL = OFF_MISC + 16;
   static constexpr int ALLOC = TOTAL + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * PBN;
   static_assert(ALLOC <= 232448, "shared memory budget of one sm_100 CTA");
+  static_assert(B_BYTES % 1024 == 0 && OFF_B % 1024 == 0, "swizzled stages on 1 KB boundaries");
 };
 
-template <bool BF16>
+// B_KMAJOR: B is [N, K] (tn); otherwise [K, N] (nn), or [groups, K, N] with rows_per_group > 0
+// (expert GEMM: a tile's 256 rows all belong to expert (mb * 256) / rows_per_group), fed as an
+// MN-major operand in 64-column swizzle blocks.
+template <bool BF16, bool B_KMAJOR, int PBN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int group_m,
-                     int l2_hint, unsigned int* status) {
-  using L = PairLayout;
+                     int l2_hint, int rows_per_group, unsigned int* status) {
+  using L = PairLayout<PBN>;
+  constexpr int P_STAGES = L::STAGES;
+  constexpr int P_BN = PBN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);  // leader's counts both CTAs
@@ -360,7 +368,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_holder)),
-                 "r"(512)
+                 "r"(L::TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
@@ -402,16 +410,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* da = smem + L::OFF_A + stage * L::A_BYTES;
           uint8_t* db = smem + L::OFF_B + stage * L::B_BYTES;
           const int ya = mb * P_BM + static_cast<int>(rank) * 128;
-          const int yb = nb * P_BN + static_cast<int>(rank) * 128;
+          const int yb = nb * P_BN + static_cast<int>(rank) * (P_BN / 2);
           if (l2_hint & 1) {
             tma_load_2d_pair_hint(&tmA, bar0, da, kb * BK, ya, pol_a);
           } else {
             tma_load_2d_pair(&tmA, bar0, da, kb * BK, ya);
           }
-          if (l2_hint & 2) {
-            tma_load_2d_pair_hint(&tmB, bar0, db, kb * BK, yb, pol_b);
+          if constexpr (B_KMAJOR) {
+            if (l2_hint & 2) {
+              tma_load_2d_pair_hint(&tmB, bar0, db, kb * BK, yb, pol_b);
+            } else {
+              tma_load_2d_pair(&tmB, bar0, db, kb * BK, yb);
+            }
           } else {
-            tma_load_2d_pair(&tmB, bar0, db, kb * BK, yb);
+            // [K, N] (or expert e's [K, N]): this CTA's PBN / 2 columns as 64-column blocks
+            const int e = rows_per_group > 0 ? (mb * P_BM) / rows_per_group : -1;
+#pragma unroll
+            for (int j = 0; j < P_BN / 128; ++j) {
+              uint8_t* dj = db + j * (64 * BK * 2);
+              if (e < 0) {
+                tma_load_2d_pair(&tmB, bar0, dj, yb + j * 64, kb * BK);
+              } else {
+                tma_load_3d_pair(&tmB, bar0, dj, yb + j * 64, kb * BK, e);
+              }
+            }
           }
           if (++stage == P_STAGES) {
             stage = 0;
@@ -424,7 +446,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ---------------- MMA issuer (leader only) ----------------
     if (leader && lane == 0) {
       constexpr uint32_t fmt = BF16 ? 1u : 0u;
-      constexpr uint32_t idesc = make_idesc(P_BM, P_BN, fmt, fmt, 0u, 0u);
+      constexpr uint32_t idesc = make_idesc(P_BM, P_BN, fmt, fmt, 0u, B_KMAJOR ? 0u : 1u);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -444,8 +466,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t b0 = smem_u32(smem + L::OFF_B + stage * L::B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
-            umma_f16_pair(d_tmem, sdesc_sw128(a0 + k * UMMA_K * 2, 16, 1024),
-                          sdesc_sw128(b0 + k * UMMA_K * 2, 16, 1024), idesc,
+            // MN-major B: K rows 128 B apart (16 per MMA), 64-column blocks 8 KB apart
+            const uint64_t bd = B_KMAJOR ? sdesc_sw128(b0 + k * UMMA_K * 2, 16, 1024)
+                                         : sdesc_sw128(b0 + k * UMMA_K * 128, 64 * BK * 2, 1024);
+            umma_f16_pair(d_tmem, sdesc_sw128(a0 + k * UMMA_K * 2, 16, 1024), bd, idesc,
                           (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_pair(&empty[stage]);  // frees this stage in both CTAs
@@ -530,7 +554,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   pair_sync();  // the leader's MMAs into this CTA's TMEM and remote arrivals are over
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::TMEM_COLS)
                  : "memory");
   }
 }
@@ -873,10 +898,13 @@ inline void pair_raster_env(int& group_m, int& l2_hint) {
   if (const char* h = std::getenv("KTA_GEMM_L2HINT")) l2_hint = std::atoi(h) & 7;
 }
 
-template <bool BF16>
+// groups > 0 (expert GEMM, B [K, N] layout only): B is [groups, K, N] and rows
+// [g * M / groups, (g + 1) * M / groups) of A and C use B[g]; M / groups must be a multiple
+// of the 256-row pair tile.
+template <bool BF16, bool B_KMAJOR, int PBN>
 int launch_pair(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda,
-                int64_t ldb, int64_t ldc, cudaStream_t stream) {
-  using L = PairLayout;
+                int64_t ldb, int64_t ldc, cudaStream_t stream, int groups = 0) {
+  using L = PairLayout<PBN>;
   const CUtensorMapDataType dt =
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb, tc;
@@ -887,10 +915,24 @@ int launch_pair(const void* A, const void* B, void* C, int M, int N, int K, int6
     int s = encode_tmap(&ta, dt, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != KTA_OK) return s;
   }
-  {
+  if (B_KMAJOR) {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
-    const uint32_t box[2] = {BK, 128};
+    const uint32_t box[2] = {BK, PBN / 2};
+    int s = encode_tmap(&tb, dt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  } else if (groups > 0) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K),
+                              static_cast<uint64_t>(groups)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ldb) * 2,
+                                 static_cast<uint64_t>(ldb) * 2 * static_cast<uint64_t>(K)};
+    const uint32_t box[3] = {64, BK, 1};
+    int s = encode_tmap(&tb, dt, 3, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != KTA_OK) return s;
+  } else {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t box[2] = {64, BK};
     int s = encode_tmap(&tb, dt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != KTA_OK) return s;
   }
@@ -901,29 +943,33 @@ int launch_pair(const void* A, const void* B, void* C, int M, int N, int K, int6
     int s = encode_tmap(&tc, dt, 2, C, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != KTA_OK) return s;
   }
-  auto kernel = gemm_pair_kernel<BF16>;
+  auto kernel = gemm_pair_kernel<BF16, B_KMAJOR, PBN>;
   int s = set_smem(kernel, L::ALLOC);
   if (s != KTA_OK) return s;
-  const int tiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+  const int tiles = ((M + P_BM - 1) / P_BM) * ((N + PBN - 1) / PBN);
   const int pairs = std::max(1, std::min(tiles, current_sm_count() / 2));
   int group_m = P_GROUP_M, l2_hint = 1;
   pair_raster_env(group_m, l2_hint);
+  const int rows_per_group = groups > 0 ? M / groups : 0;
   return launch_ex(kernel, dim3(static_cast<unsigned>(2 * pairs)), dim3(NUM_THREADS), L::ALLOC,
-                   stream, 2, ta, tb, tc, M, N, K, group_m, l2_hint, device_status_ptr());
+                   stream, 2, ta, tb, tc, M, N, K, group_m, l2_hint, rows_per_group,
+                   device_status_ptr());
 }
 
-// Estimated relative time of a tile width: waves x columns, discounted by how close the
-// tile runs to the shared-memory bandwidth limit (128x64 tiles feed the tensor core at
-// 192 B/clk against 128 B/clk available; 128x128 at 128; 128x256 at 96).
+// Estimated relative time of a tile width: waves x columns, discounted by the shared-memory
+// traffic per tensor cycle (operand reads plus the TMA's writes: 128x256 tiles 192 B/clk,
+// 128x128 256, 128x64 384). Measured: 128x128 tiles of a 4096^3 nn GEMM ran at 0.68 of the
+// 128x256 rate.
 inline double tile_cost(int M, int N, int BN, int sms) {
-  const double eff = BN == 256 ? 1.0 : (BN == 128 ? 0.9 : 0.6);
+  const double eff = BN == 256 ? 1.0 : (BN == 128 ? 0.72 : 0.5);
   const long tiles = static_cast<long>((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const long waves = (tiles + sms - 1) / sms;
   return static_cast<double>(waves) * BN / eff;
 }
 
-// Selection of the 2-SM path: KTA_GEMM_PAIR=0 never, =force always (tn, M >= 129),
-// unset: when its 256x256 tiles fill the machine about as well as 128x256 ones.
+// Selection of the 2-SM path: KTA_GEMM_PAIR=0 never; =force always (M >= 129; nn and expert
+// GEMMs with 256-row multiples per expert included); unset: tn GEMMs whose 256x256 tiles
+// fill the machine about as well as single-SM tiles.
 inline int pair_mode() {
   const char* v = std::getenv("KTA_GEMM_PAIR");
   if (v == nullptr) return 1;
@@ -961,18 +1007,20 @@ int dispatch(const void* A, const void* B, void* C, int64_t M64, int64_t N64, in
     return launch_skinny<64, BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
   }
   const int sms = std::max(1, current_sm_count());
-  const int mode = B_KMAJOR ? pair_mode() : 0;
+  const int mode = pair_mode();
   if (mode == 2 && M > 128 && sms >= 2) {
-    return launch_pair<BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+    return launch_pair<BF16, B_KMAJOR, 256>(A, B, C, M, N, K, lda, ldb, ldc, stream);
   }
-  if (mode == 1 && sms >= 2) {
+  // By default only tn takes pairs: with B an MN-major operand the pair kernel ran 8-10 %
+  // below 128x256 single-SM tiles at 6144^3 and 8192^3 (it wins for tn: 1335 vs 1239)
+  if (B_KMAJOR && mode == 1 && sms >= 2) {
     // 2-SM 256x256 tiles when they fill the machine about as well as 128x256 ones
     const long pair_tiles = static_cast<long>((M + 255) / 256) * ((N + 255) / 256);
     const long pair_waves = (pair_tiles + sms / 2 - 1) / (sms / 2);
     const long one_tiles = static_cast<long>((M + 127) / 128) * ((N + 255) / 256);
     const long one_waves = (one_tiles + sms - 1) / sms;
     if (pair_tiles >= sms / 2 && pair_waves <= one_waves) {
-      return launch_pair<BF16>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+      return launch_pair<BF16, B_KMAJOR, 256>(A, B, C, M, N, K, lda, ldb, ldc, stream);
     }
   }
   const double c256 = tile_cost(M, N, 256, sms);
@@ -1008,6 +1056,11 @@ int moe_dispatch(const void* A, const void* W, void* C, int64_t E64, int64_t T64
             K = static_cast<int>(K64);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   const int sms = std::max(1, current_sm_count());
+  // 2-SM 256 x 128 tiles (both CTAs' rows in one expert) only with KTA_GEMM_PAIR=force: at
+  // the test-set shape they ran at 530 TFLOP/s against 597 for single-SM tiles
+  if (pair_mode() == 2 && (T / E) % P_BM == 0 && sms >= 2) {
+    return launch_pair<BF16, false, 128>(A, W, C, T, N, K, K, N, N, stream, E);
+  }
   if (tile_cost(T, N, 256, sms) <= tile_cost(T, N, 128, sms)) {
     return launch_main<256, 4, BF16, false>(A, W, C, T, N, K, K, N, N, stream, E);
   }

@@ -498,6 +498,15 @@ __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_t bar_cluster,
+                                                 void* dst, int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // The same load with an L2 eviction-priority policy (createpolicy) for the fetched lines.
 __device__ __forceinline__ void tma_load_2d_pair_hint(const CUtensorMap* map, uint32_t bar_cluster,
                                                       void* dst, int32_t x, int32_t y,

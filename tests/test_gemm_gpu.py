@@ -141,6 +141,26 @@ def test_gemm_pair_kernel_ragged(cuda_device, monkeypatch, m, n, k, dtype, route
     _check(c, ogemm.gemm_tn(a.double().numpy(), b.double().numpy()))
 
 
+@pytest.mark.parametrize("route", ["default", "force", "off"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
+def test_gemm_nn_pair_kernel_ragged(cuda_device, monkeypatch, m, n, k, dtype, route):
+    """The reference's layout C = A @ B (B [K, N], an MN-major operand in 64-column blocks)
+    through the 2-SM pair kernel on ragged edges, by the default routing, KTA_GEMM_PAIR=force
+    and, for comparison, the one-SM kernel (KTA_GEMM_PAIR=0)."""
+    from kta_b200 import ops
+
+    if route == "default":
+        monkeypatch.delenv("KTA_GEMM_PAIR", raising=False)
+    else:
+        monkeypatch.setenv("KTA_GEMM_PAIR", "force" if route == "force" else "0")
+    a, b = _inputs(m, n, k, dtype, seed=5, b_layout="kn")
+    c = torch.full((m, n), float("nan"), dtype=dtype, device=cuda_device)
+    ops.gemm(a.to(cuda_device), b.to(cuda_device), out=c, b_layout="kn")
+    torch.cuda.synchronize()
+    _check(c, ogemm.gemm_nn(a.double().numpy(), b.double().numpy()))
+
+
 @pytest.mark.parametrize("route", ["force", "off"])
 @pytest.mark.parametrize("m,n,k", [(520, 1000, 136), (129, 384, 64), (700, 904, 320)])
 def test_gemm_small_shapes_on_both_kernels(cuda_device, monkeypatch, m, n, k, route):

@@ -29,13 +29,23 @@ def _check(c, ref):
     assert not bad.any(), f"{int(bad.sum())} mismatches, max err {err.max():.3e}"
 
 
+# Routes: "default" (2-SM 256 x 128 pair tiles when every expert's rows are a multiple of 256
+# and the pair grid takes no more waves, else 128-row tiles on single SMs), "0"
+# (KTA_GEMM_PAIR=0: single SMs), "force" (pairs whenever the rows allow). Experts of 512 and
+# 256 rows with ragged N (520, 264) and K tails (200, 72) reach the pair kernel.
+@pytest.mark.parametrize("route", ["default", "0", "force"])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("e,t,n,k", [(1, 128, 64, 64), (2, 256, 256, 128), (4, 512, 520, 200),
                                      (3, 384, 1024, 1000), (8, 2048, 1024, 2048),
-                                     (8, 1024, 768, 4096)])
-def test_moe_gemm(cuda_device, e, t, n, k, dtype):
+                                     (8, 1024, 768, 4096), (2, 1024, 520, 200),
+                                     (4, 1024, 264, 72)])
+def test_moe_gemm(cuda_device, monkeypatch, e, t, n, k, dtype, route):
     from kta_b200 import ops
 
+    if route == "default":
+        monkeypatch.delenv("KTA_GEMM_PAIR", raising=False)
+    else:
+        monkeypatch.setenv("KTA_GEMM_PAIR", route)
     a, w = _inputs(e, t, n, k, dtype)
     c = ops.moe_gemm(a.to(cuda_device), w.to(cuda_device))
     torch.cuda.synchronize()
@@ -51,6 +61,21 @@ def test_moe_experts_are_not_mixed(cuda_device):
     c = ops.moe_gemm(a.to(cuda_device), w.to(cuda_device)).cpu()
     assert torch.count_nonzero(c[:256]) == 0 and torch.count_nonzero(c[384:]) == 0
     assert torch.count_nonzero(c[256:384]) > 0
+
+
+def test_moe_experts_are_not_mixed_pair_tiles(cuda_device, monkeypatch):
+    """The same with 256-row experts, on the 2-SM pair kernel: a pair tile's 256 rows and both
+    CTAs' halves of W belong to one expert."""
+    from kta_b200 import ops
+
+    monkeypatch.setenv("KTA_GEMM_PAIR", "force")
+    a, w = _inputs(4, 1024, 384, 256, torch.bfloat16, seed=4)
+    w[[0, 1, 3]] = 0
+    c = ops.moe_gemm(a.to(cuda_device), w.to(cuda_device)).cpu()
+    assert torch.count_nonzero(c[:512]) == 0 and torch.count_nonzero(c[768:]) == 0
+    assert torch.count_nonzero(c[512:768]) > 0
+    ref = ogemm.moe_gemm(a.double().numpy(), w.double().numpy())
+    _check(c, ref)
 
 
 def test_moe_nan_fill_and_so_shim(cuda_device):
