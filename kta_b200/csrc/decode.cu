@@ -361,44 +361,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (last) __threadfence();
         }
         last = __shfl_sync(0xffffffffu, last, 0);
-        constexpr int NC = 4;  // contributors combined with independent loads (the common case)
-        if (last && c_last - c_first < NC) {
-          // Up to four CTAs hold pieces of this pair: per head, every lane issues all their
-          // LSE and output loads at once (one L2 round trip per head instead of one per
-          // contributor and element).
-          int sl[NC];
-          bool on[NC];
-#pragma unroll
-          for (int j = 0; j < NC; ++j) {
-            const int c = c_first + j;
-            on[j] = c <= c_last && w.busy(c);
-            sl[j] = on[j] ? 2 * c + (w.start(c) >= sg.pair_start ? 0 : 1) : 0;
-          }
+        if (last) {
+          // The pieces of this pair's CTAs [c_first, c_last] (idle ones hold none), per head:
+          // four contributors at a time with all their LSE and output loads issued at once,
+          // a running maximum rescaling the sums between groups (one L2 round trip per group
+          // and head, however many CTAs the pair spans).
+          constexpr int NC = 4;
+          const int ncon = c_last - c_first + 1;
           for (int g = 0; g < G; ++g) {
-            float lse[NC], ov[NC][D / 32];
-#pragma unroll
-            for (int j = 0; j < NC; ++j) {
-              lse[j] = on[j] ? __ldcg(p.part_lse + sl[j] * G + g) : -INFINITY;
-#pragma unroll
-              for (int u = 0; u < D / 32; ++u) {
-                ov[j][u] = on[j] ? __ldcg(p.part_o + (static_cast<long long>(sl[j]) * G + g) * D +
-                                          u * 32 + lane)
-                                 : 0.f;
-              }
-            }
-            float mx = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < NC; ++j) mx = fmaxf(mx, lse[j]);
-            float wsum = 0.f, acc[D / 32];
+            float mx = -INFINITY, wsum = 0.f, acc[D / 32];
 #pragma unroll
             for (int u = 0; u < D / 32; ++u) acc[u] = 0.f;
-            if (mx != -INFINITY) {
+            for (int j0 = 0; j0 < ncon; j0 += NC) {
+              float lse[NC], ov[NC][D / 32];
 #pragma unroll
               for (int j = 0; j < NC; ++j) {
-                const float wt = (lse[j] == -INFINITY) ? 0.f : exp2f(lse[j] - mx);
-                wsum += wt;
+                const int c = c_first + j0 + j;
+                const bool on = j0 + j < ncon && w.busy(c);
+                const int sl = on ? 2 * c + (w.start(c) >= sg.pair_start ? 0 : 1) : 0;
+                lse[j] = on ? __ldcg(p.part_lse + sl * G + g) : -INFINITY;
 #pragma unroll
-                for (int u = 0; u < D / 32; ++u) acc[u] += wt * ov[j][u];
+                for (int u = 0; u < D / 32; ++u) {
+                  ov[j][u] = on ? __ldcg(p.part_o + (static_cast<long long>(sl) * G + g) * D +
+                                         u * 32 + lane)
+                                : 0.f;
+                }
+              }
+              float cmx = -INFINITY;
+#pragma unroll
+              for (int j = 0; j < NC; ++j) cmx = fmaxf(cmx, lse[j]);
+              const float nmx = fmaxf(mx, cmx);
+              if (nmx != -INFINITY) {
+                const float sc = (mx == -INFINITY) ? 0.f : exp2f(mx - nmx);
+                wsum *= sc;
+#pragma unroll
+                for (int u = 0; u < D / 32; ++u) acc[u] *= sc;
+#pragma unroll
+                for (int j = 0; j < NC; ++j) {
+                  const float wt = (lse[j] == -INFINITY) ? 0.f : exp2f(lse[j] - nmx);
+                  wsum += wt;
+#pragma unroll
+                  for (int u = 0; u < D / 32; ++u) acc[u] += wt * ov[j][u];
+                }
+                mx = nmx;
               }
             }
 #pragma unroll
@@ -406,30 +411,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               p.out[(static_cast<long long>(sg.b) * p.hq + sg.kvh * G + g) * D + u * 32 + lane] =
                   __float2bfloat16_rn(wsum > 0.f ? acc[u] / wsum : 0.f);
             }
-          }
-          if (lane == 0) p.counters[pair] = 0u;  // ready for the next call
-        } else if (last) {
-          for (int idx = lane; idx < G * D; idx += 32) {
-            const int g = idx / D, d = idx - g * D;
-            float mx = -INFINITY;
-            for (int c = c_first; c <= c_last; ++c) {
-              if (!w.busy(c)) continue;
-              const int sl = 2 * c + (w.start(c) >= sg.pair_start ? 0 : 1);
-              mx = fmaxf(mx, __ldcg(p.part_lse + sl * G + g));
-            }
-            float wsum = 0.f, acc = 0.f;
-            if (mx != -INFINITY) {
-              for (int c = c_first; c <= c_last; ++c) {
-                if (!w.busy(c)) continue;
-                const int sl = 2 * c + (w.start(c) >= sg.pair_start ? 0 : 1);
-                const float lse = __ldcg(p.part_lse + sl * G + g);
-                const float wt = (lse == -INFINITY) ? 0.f : exp2f(lse - mx);
-                wsum += wt;
-                acc += wt * __ldcg(p.part_o + (static_cast<long long>(sl) * G + g) * D + d);
-              }
-            }
-            p.out[(static_cast<long long>(sg.b) * p.hq + sg.kvh * G + g) * D + d] =
-                __float2bfloat16_rn(wsum > 0.f ? acc / wsum : 0.f);
           }
           if (lane == 0) p.counters[pair] = 0u;  // ready for the next call
         }

@@ -88,6 +88,17 @@ def test_decode_splits_across_ctas(cuda_device, lengths, entry):
 
 
 @pytest.mark.parametrize("entry", ENTRIES)
+def test_decode_one_rank_of_eight(cuda_device, entry):
+    """The first 8 of the benchmark's 64 lengths U[1024, 8192] (one GPU's share at eight GPUs): each
+    CTA holds about 12 tiles, so a long sequence's pair is split over five to seven CTAs and
+    the last one combines more than four pieces."""
+    lengths = np.random.default_rng(0).integers(1024, 8193, size=64)[:8]
+    q, kc, vc, ln, off = _make(lengths, seed=8)
+    out = _run(cuda_device, q, kc, vc, ln, off, 8192, entry=entry)
+    _check(out, q, kc, vc, ln, off)
+
+
+@pytest.mark.parametrize("entry", ENTRIES)
 def test_decode_gaps_between_sequences(cuda_device, entry):
     """Sequences need not be packed back to back: rows between them are never read."""
     q, kc, vc, ln, off = _make([700, 513, 2], gap=37)
