@@ -19,7 +19,9 @@
 //     operand with movmatrix, O^T += V^T P^T; tensor time is far below the KV stream;
 //   * at the end of a segment the compute warps drop their (m, l, O) into shared memory and
 //     continue at once: a merger warp folds the eight states and writes the output or the
-//     partial, so merges never stall the KV stream;
+//     partial, so merges never stall the KV stream; the CTA's last segment, which ends the
+//     stream, the eight compute warps fold themselves (and combine the pair when this CTA
+//     is its last contributor), 256 threads instead of one warp on the kernel's tail;
 //   * every mbarrier wait is bounded; out-of-range lengths/offsets are rejected on the
 //     device (status KTA_ERR_DEVICE_BOUNDS) and that sequence's output is zero-filled.
 #include <algorithm>
@@ -51,6 +53,7 @@ enum : unsigned int {
   SITE_CONS_FULL = 0x302,
   SITE_CONS_MFREE = 0x303,
   SITE_MERGE_FULL = 0x304,
+  SITE_CONS_GROUP = 0x305,
 };
 
 struct Params {
@@ -75,7 +78,7 @@ struct Smem {
     off_tiles = off_merge_ml + COMPUTE_WARPS * G * 2 * 4;     // [B] tiles per pair, -1 bad
     off_prefix = off_tiles + B * 4;                           // [B + 1] tiles before b
     off_bar = ((off_prefix + (B + 1) * 4 + 7) / 8) * 8;
-    off_misc = off_bar + (2 * stages + 2) * 8;
+    off_misc = off_bar + (2 * stages + 3) * 8;
     total = off_misc + 32;
   }
 };
@@ -167,6 +170,165 @@ __device__ __forceinline__ Segment segment_at(const Work& w, long long t, long l
   return s;
 }
 
+// The threads that fold a segment's eight warp states: the merger warp (segments that end
+// while the CTA still streams) or the eight compute warps (the CTA's last segment, when they
+// have nothing else to do). sync() orders the group's shared- and global-memory writes before
+// every member's later accesses; the compute warps' version waits on an mbarrier with the
+// library's bounded wait, so a member that gave up never leaves the others waiting.
+struct WarpGroup {
+  static constexpr int THREADS = 32;
+  int ti;
+  __device__ __forceinline__ bool sync() {
+    __syncwarp();
+    return true;
+  }
+};
+struct ComputeGroup {
+  static constexpr int THREADS = COMPUTE_WARPS * 32;
+  int ti;
+  uint64_t* bar;  // count COMPUTE_WARPS: one arrival per warp
+  uint32_t phase;
+  volatile int* abort;
+  unsigned int* status;
+  __device__ __forceinline__ bool sync() {
+    __syncwarp();
+    if ((ti & 31) == 0) mbar_arrive(bar);
+    const bool ok = mbar_wait(bar, phase, abort, status, SITE_CONS_GROUP);
+    phase ^= 1u;
+    return ok;
+  }
+};
+
+// Folds segment sg's eight warp states (merge_o [warps][G][D], merge_ml [warps][G][2] = m, l)
+// into the output of a whole pair, or into partial slot `slot` (normalised O and the LSE in
+// log2 units) of a split one. Thread g < G turns head g's states into one normalised weight
+// per warp, written over that warp's m, and the head's LSE, written over warp 0's l (only
+// thread g touches head g's entries); every element is then a weighted sum of eight values.
+template <typename Group>
+__device__ bool fold_segment(Group& grp, const Params& p, const Segment& sg, bool partial,
+                             int slot, int G, float* merge_o, float* merge_ml) {
+  for (int g = grp.ti; g < G; g += Group::THREADS) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int wi = 0; wi < COMPUTE_WARPS; ++wi) M = fmaxf(M, merge_ml[(wi * G + g) * 2]);
+    float fw[COMPUTE_WARPS];
+    float Lsum = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < COMPUTE_WARPS; ++wi) {
+      const float mw = merge_ml[(wi * G + g) * 2];
+      fw[wi] = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      Lsum += merge_ml[(wi * G + g) * 2 + 1] * fw[wi];
+    }
+    const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+#pragma unroll
+    for (int wi = 0; wi < COMPUTE_WARPS; ++wi) merge_ml[(wi * G + g) * 2] = fw[wi] * inv;
+    merge_ml[g * 2 + 1] = Lsum > 0.f ? M + __log2f(Lsum) : -INFINITY;
+  }
+  if (!grp.sync()) return false;
+  for (int idx = grp.ti; idx < G * D; idx += Group::THREADS) {
+    const int g = idx / D, d = idx - g * D;
+    float val = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < COMPUTE_WARPS; ++wi) {
+      val += merge_o[(wi * G + g) * D + d] * merge_ml[(wi * G + g) * 2];
+    }
+    if (!partial) {
+      p.out[(static_cast<long long>(sg.b) * p.hq + sg.kvh * G + g) * D + d] =
+          __float2bfloat16_rn(val);
+    } else {
+      p.part_o[(static_cast<long long>(slot) * G + g) * D + d] = val;
+      if (d == 0) p.part_lse[slot * G + g] = merge_ml[g * 2 + 1];
+    }
+  }
+  return true;
+}
+
+// After a split segment's partial stores: counts this CTA's arrival on the pair, and the last
+// of the pair's CTAs combines every piece (decode_combine): contributors four at a time with
+// all their loads issued at once, a running maximum rescaling the sums between groups, four
+// output elements per thread. `flag` is a shared int of this group.
+template <typename Group>
+__device__ void arrive_and_combine(Group& grp, const Params& p, const Work& w, const Segment& sg,
+                                   int G, volatile int* flag) {
+  const int pair = sg.b * p.hkv + sg.kvh;
+  const long long pair_end = sg.pair_start + sg.ntiles;
+  const int c_first = w.owner(sg.pair_start);
+  const int c_last = w.owner(pair_end - 1);
+  // every member's partial stores precede thread 0's fence, which is cumulative
+  if (!grp.sync()) return;
+  if (grp.ti == 0) {
+    int n = 0;  // CTAs holding a piece of this pair
+    for (int c = c_first; c <= c_last; ++c) n += w.busy(c) ? 1 : 0;
+    __threadfence();
+    const unsigned int prev = atomicAdd(p.counters + pair, 1u);
+    const int last = (prev == static_cast<unsigned int>(n - 1)) ? 1 : 0;
+    if (last) __threadfence();
+    *flag = last;
+  }
+  if (!grp.sync()) return;
+  if (*flag == 0) return;
+  constexpr int NC = 4, U = 4;
+  const int ncon = c_last - c_first + 1;
+  for (int base = 0; base < G * D; base += Group::THREADS * U) {
+    int gi[U], di[U];
+    bool vi[U];
+    float mx[U], wsum[U], acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = base + u * Group::THREADS + grp.ti;
+      vi[u] = e < G * D;
+      gi[u] = vi[u] ? e / D : 0;
+      di[u] = vi[u] ? e - gi[u] * D : 0;
+      mx[u] = -INFINITY;
+      wsum[u] = 0.f;
+      acc[u] = 0.f;
+    }
+    for (int j0 = 0; j0 < ncon; j0 += NC) {
+      float lse[NC][U], ov[NC][U];
+#pragma unroll
+      for (int j = 0; j < NC; ++j) {
+        const int c = c_first + j0 + j;
+        const bool on = j0 + j < ncon && w.busy(c);
+        const int sl = on ? 2 * c + (w.start(c) >= sg.pair_start ? 0 : 1) : 0;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const bool ld = on && vi[u];
+          lse[j][u] = ld ? __ldcg(p.part_lse + sl * G + gi[u]) : -INFINITY;
+          ov[j][u] = ld ? __ldcg(p.part_o + (static_cast<long long>(sl) * G + gi[u]) * D + di[u])
+                        : 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float cmx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < NC; ++j) cmx = fmaxf(cmx, lse[j][u]);
+        const float nmx = fmaxf(mx[u], cmx);
+        if (nmx != -INFINITY) {
+          const float sc = (mx[u] == -INFINITY) ? 0.f : exp2f(mx[u] - nmx);
+          wsum[u] *= sc;
+          acc[u] *= sc;
+#pragma unroll
+          for (int j = 0; j < NC; ++j) {
+            const float wt = (lse[j][u] == -INFINITY) ? 0.f : exp2f(lse[j][u] - nmx);
+            wsum[u] += wt;
+            acc[u] += wt * ov[j][u];
+          }
+          mx[u] = nmx;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (vi[u]) {
+        p.out[(static_cast<long long>(sg.b) * p.hq + sg.kvh * G + gi[u]) * D + di[u]] =
+            __float2bfloat16_rn(wsum[u] > 0.f ? acc[u] / wsum[u] : 0.f);
+      }
+    }
+  }
+  if (grp.ti == 0) p.counters[pair] = 0u;  // ready for the next call
+}
+
 // NT = number of 8-wide query-head tiles (1: G <= 8, 2: G <= 16).
 template <int STAGES, int NT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -183,7 +345,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* mfull = empty + STAGES;   // compute warps -> merger: states are in smem
   uint64_t* mfree = mfull + 1;        // merger -> compute warps: merge area is free
+  uint64_t* csync = mfree + 1;        // the compute warps among themselves (last segment)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.off_misc);
+  volatile int* merger_flag = abort_flag + 2;   // "this CTA combines the pair" for the merger
+  volatile int* compute_flag = abort_flag + 3;  // ... and for the compute warps
 
   const int warp = warp_id();
   const int lane = threadIdx.x & 31;
@@ -208,6 +373,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(mfull, COMPUTE_WARPS);
     mbar_init(mfree, 1);
+    mbar_init(csync, COMPUTE_WARPS);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -293,128 +459,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else if (warp == MERGER_WARP) {
     // ------------------------------ merger ------------------------------
+    // Segments that end while the CTA still streams; the CTA's last segment is folded by the
+    // compute warps themselves, which are idle by then.
+    WarpGroup grp{lane};
     int seg = 0;
     for (long long t = my_begin; t < my_end; ++seg) {
       const Segment sg = segment_at(w, t, my_end);
+      if (sg.next >= my_end) break;
       if (!mbar_wait(mfull, static_cast<uint32_t>(seg & 1), abort_flag, p.status,
                      SITE_MERGE_FULL)) {
         break;
       }
       const bool partial = !(sg.i0 == 0 && sg.i1 == sg.ntiles);
-      const int pair = sg.b * p.hkv + sg.kvh;
       // Slot of a partial segment: the CTA's first segment uses 2c, its last 2c + 1.
       const int slot = 2 * static_cast<int>(blockIdx.x) + (t == my_begin ? 0 : 1);
-      // Lane g < G folds head g's eight (m, l) states into one normalised weight per warp,
-      // written over that warp's m (only lane g touches head g's entries), and keeps the
-      // head's log2-sum-exp; every output element is then a weighted sum of eight values.
-      float lse_g = -INFINITY;
-      for (int g = lane; g < G; g += 32) {
-        float M = -INFINITY;
-#pragma unroll
-        for (int wi = 0; wi < COMPUTE_WARPS; ++wi) M = fmaxf(M, merge_ml[(wi * G + g) * 2]);
-        float fw[COMPUTE_WARPS];
-        float Lsum = 0.f;
-#pragma unroll
-        for (int wi = 0; wi < COMPUTE_WARPS; ++wi) {
-          const float mw = merge_ml[(wi * G + g) * 2];
-          fw[wi] = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-          Lsum += merge_ml[(wi * G + g) * 2 + 1] * fw[wi];
-        }
-        const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
-#pragma unroll
-        for (int wi = 0; wi < COMPUTE_WARPS; ++wi) merge_ml[(wi * G + g) * 2] = fw[wi] * inv;
-        lse_g = Lsum > 0.f ? M + __log2f(Lsum) : -INFINITY;
-      }
-      __syncwarp();
-      for (int idx = lane; idx < G * D; idx += 32) {
-        const int g = idx / D, d = idx - g * D;  // g is the same for the 32 lanes (D = 128)
-        float val = 0.f;
-#pragma unroll
-        for (int wi = 0; wi < COMPUTE_WARPS; ++wi) {
-          val += merge_o[(wi * G + g) * D + d] * merge_ml[(wi * G + g) * 2];
-        }
-        const float lse = __shfl_sync(0xffffffffu, lse_g, g);
-        if (!partial) {
-          p.out[(static_cast<long long>(sg.b) * p.hq + sg.kvh * G + g) * D + d] =
-              __float2bfloat16_rn(val);
-        } else {
-          p.part_o[(static_cast<long long>(slot) * G + g) * D + d] = val;
-          if (d == 0) p.part_lse[slot * G + g] = lse;
-        }
-      }
+      fold_segment(grp, p, sg, partial, slot, G, merge_o, merge_ml);
       __syncwarp();
       if (lane == 0) mbar_arrive(mfree);  // the merge area may be overwritten
-      if (partial) {
-        // Release every lane's partial stores (the warp barrier orders them before lane 0's
-        // fence, which is cumulative), count the arrival, and let the last contributor of
-        // the pair combine all of them (decode_combine).
-        const long long pair_end = sg.pair_start + sg.ntiles;
-        const int c_first = w.owner(sg.pair_start);
-        const int c_last = w.owner(pair_end - 1);
-        int last = 0;
-        if (lane == 0) {
-          int n = 0;  // CTAs holding a piece of this pair
-          for (int c = c_first; c <= c_last; ++c) n += w.busy(c) ? 1 : 0;
-          __threadfence();
-          const unsigned int prev = atomicAdd(p.counters + pair, 1u);
-          last = (prev == static_cast<unsigned int>(n - 1)) ? 1 : 0;
-          if (last) __threadfence();
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          // The pieces of this pair's CTAs [c_first, c_last] (idle ones hold none), per head:
-          // four contributors at a time with all their LSE and output loads issued at once,
-          // a running maximum rescaling the sums between groups (one L2 round trip per group
-          // and head, however many CTAs the pair spans).
-          constexpr int NC = 4;
-          const int ncon = c_last - c_first + 1;
-          for (int g = 0; g < G; ++g) {
-            float mx = -INFINITY, wsum = 0.f, acc[D / 32];
-#pragma unroll
-            for (int u = 0; u < D / 32; ++u) acc[u] = 0.f;
-            for (int j0 = 0; j0 < ncon; j0 += NC) {
-              float lse[NC], ov[NC][D / 32];
-#pragma unroll
-              for (int j = 0; j < NC; ++j) {
-                const int c = c_first + j0 + j;
-                const bool on = j0 + j < ncon && w.busy(c);
-                const int sl = on ? 2 * c + (w.start(c) >= sg.pair_start ? 0 : 1) : 0;
-                lse[j] = on ? __ldcg(p.part_lse + sl * G + g) : -INFINITY;
-#pragma unroll
-                for (int u = 0; u < D / 32; ++u) {
-                  ov[j][u] = on ? __ldcg(p.part_o + (static_cast<long long>(sl) * G + g) * D +
-                                         u * 32 + lane)
-                                : 0.f;
-                }
-              }
-              float cmx = -INFINITY;
-#pragma unroll
-              for (int j = 0; j < NC; ++j) cmx = fmaxf(cmx, lse[j]);
-              const float nmx = fmaxf(mx, cmx);
-              if (nmx != -INFINITY) {
-                const float sc = (mx == -INFINITY) ? 0.f : exp2f(mx - nmx);
-                wsum *= sc;
-#pragma unroll
-                for (int u = 0; u < D / 32; ++u) acc[u] *= sc;
-#pragma unroll
-                for (int j = 0; j < NC; ++j) {
-                  const float wt = (lse[j] == -INFINITY) ? 0.f : exp2f(lse[j] - nmx);
-                  wsum += wt;
-#pragma unroll
-                  for (int u = 0; u < D / 32; ++u) acc[u] += wt * ov[j][u];
-                }
-                mx = nmx;
-              }
-            }
-#pragma unroll
-            for (int u = 0; u < D / 32; ++u) {
-              p.out[(static_cast<long long>(sg.b) * p.hq + sg.kvh * G + g) * D + u * 32 + lane] =
-                  __float2bfloat16_rn(wsum > 0.f ? acc[u] / wsum : 0.f);
-            }
-          }
-          if (lane == 0) p.counters[pair] = 0u;  // ready for the next call
-        }
-      }
+      if (partial) arrive_and_combine(grp, p, w, sg, G, merger_flag);
       t = sg.next;
     }
     __syncwarp();
@@ -576,6 +638,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
           }
         }
+      }
+      if (sg.next >= my_end) {
+        // The CTA's last segment: the eight compute warps fold it (and combine the pair if
+        // this CTA is its last contributor) instead of handing it to the merger warp.
+        ComputeGroup grp{static_cast<int>(threadIdx.x), csync, 0u, abort_flag, p.status};
+        if (grp.sync()) {  // every warp's state is in shared memory
+          const bool partial = !(sg.i0 == 0 && sg.i1 == sg.ntiles);
+          const int slot = 2 * static_cast<int>(blockIdx.x) + (t == my_begin ? 0 : 1);
+          if (fold_segment(grp, p, sg, partial, slot, G, merge_o, merge_ml) && partial) {
+            arrive_and_combine(grp, p, w, sg, G, compute_flag);
+          }
+        }
+        break;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(mfull);
