@@ -177,6 +177,8 @@ __device__ __forceinline__ Segment segment_at(const Work& w, long long t, long l
 // library's bounded wait, so a member that gave up never leaves the others waiting.
 struct WarpGroup {
   static constexpr int THREADS = 32;
+  static constexpr int COMBINE_NC = 4;  // pieces whose loads go out together
+  static constexpr int COMBINE_U = 8;   // output elements per thread and pass
   int ti;
   __device__ __forceinline__ bool sync() {
     __syncwarp();
@@ -185,6 +187,8 @@ struct WarpGroup {
 };
 struct ComputeGroup {
   static constexpr int THREADS = COMPUTE_WARPS * 32;
+  static constexpr int COMBINE_NC = 8;
+  static constexpr int COMBINE_U = 2;
   int ti;
   uint64_t* bar;  // count COMPUTE_WARPS: one arrival per warp
   uint32_t phase;
@@ -244,9 +248,12 @@ __device__ bool fold_segment(Group& grp, const Params& p, const Segment& sg, boo
 }
 
 // After a split segment's partial stores: counts this CTA's arrival on the pair, and the last
-// of the pair's CTAs combines every piece (decode_combine): contributors four at a time with
-// all their loads issued at once, a running maximum rescaling the sums between groups, four
-// output elements per thread. `flag` is a shared int of this group.
+// of the pair's CTAs combines every piece (decode_combine): Group::COMBINE_NC contributors at
+// a time with all their loads issued at once, a running maximum rescaling the sums between
+// groups, Group::COMBINE_U output elements per thread and pass (the warp: 4 pieces x 8
+// elements, two passes for G = 4; the compute warps: 8 pieces x 2 elements, one pass), so a
+// pair spread over up to eight CTAs costs one or two L2 round trips per pass. `flag` is a
+// shared int of this group.
 template <typename Group>
 __device__ void arrive_and_combine(Group& grp, const Params& p, const Work& w, const Segment& sg,
                                    int G, volatile int* flag) {
@@ -267,7 +274,7 @@ __device__ void arrive_and_combine(Group& grp, const Params& p, const Work& w, c
   }
   if (!grp.sync()) return;
   if (*flag == 0) return;
-  constexpr int NC = 4, U = 4;
+  constexpr int NC = Group::COMBINE_NC, U = Group::COMBINE_U;
   const int ncon = c_last - c_first + 1;
   for (int base = 0; base < G * D; base += Group::THREADS * U) {
     int gi[U], di[U];
