@@ -83,3 +83,24 @@ def test_attn_nan_fill_coverage_and_determinism(cuda_device):
     assert not torch.isnan(o1).any() and not torch.isnan(l1).any()
     assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
     assert torch.equal(l1, l2)
+
+
+@pytest.mark.parametrize("b,s,h", [(1, 4096, 32), (2, 1000, 6)])
+def test_attn_unit_orders_give_identical_bits(cuda_device, monkeypatch, b, s, h):
+    """Head-major and cost-major unit orders (KTA_ATTN_ORDER) change which CTA runs a unit
+    and when, not its arithmetic: O and LSE are bitwise the same, and match the oracle on a
+    few heads. B=1 S=4096 H=32 is one GPU's share of the benchmark at eight GPUs (cost-major
+    by default); the ragged case has an odd number of query tiles."""
+    from kta_b200 import ops
+
+    q, k, v = (t.to(cuda_device) for t in _make(b, s, h, seed=7))
+    out = {}
+    for order in ("head", "cost"):
+        monkeypatch.setenv("KTA_ATTN_ORDER", order)
+        o, lse = ops.attn_fwd_causal(q, k, v)
+        torch.cuda.synchronize()
+        out[order] = (o, lse)
+    assert torch.equal(out["head"][0].view(torch.int16), out["cost"][0].view(torch.int16))
+    assert torch.equal(out["head"][1], out["cost"][1])
+    heads = [(0, 0), (b - 1, h - 1)]
+    _check(q.cpu(), k.cpu(), v.cpu(), out["cost"][0], out["cost"][1], heads=heads)
