@@ -276,15 +276,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_ld_32x32b_x16(t + c, r);
           tmem_ld_wait();
           reg_fence(r);
+          if (c + 16 == COLS) {
+            // the buffer's last columns are in registers: hand it back before the last FMAs
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+          }
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             acc[c / 2 + i] = fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), s2,
                                   acc[c / 2 + i]);
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
         buf ^= 1;
         if (buf == 0) bphase ^= 1u;
       }
