@@ -98,7 +98,8 @@ def min_work(problem: Problem, shape: Mapping[str, Any]) -> dict[str, float]:
     raw = problem.params.get(MIN_WORK_KEY)
     if not isinstance(raw, dict) or not raw:
         raise NotSupported(
-            f"Problem {problem.name} has no params.{MIN_WORK_KEY} (unit -> expression over case.*)"
+            f"case {problem.name}: params.{MIN_WORK_KEY} is missing (it maps each hardware unit "
+            "to an expression of case.* values)"
         )
     return {str(u): float(Expr.parse(str(src), set()).eval({}, case=shape))
             for u, src in raw.items()}
@@ -118,10 +119,11 @@ def sol_us(work: Mapping[str, float], hw: HwModel) -> dict[str, float]:
 def bound(work: Mapping[str, float], hw: HwModel, case_name: str = "") -> Bound:
     missing = sorted(u for u, w in work.items() if w > 0 and hw.rate(u) is None)
     if missing:
-        raise NotSupported(f"HwModel {hw.target}@{hw.version} has no peak for units {missing}")
+        raise NotSupported(f"hardware model {hw.target}@{hw.version} gives no peak rate for "
+                           f"{missing}")
     per_unit = sol_us(work, hw)
     if not per_unit:
-        raise ValueError(f"no positive work for case {case_name}")
+        raise ValueError(f"case {case_name} declares no unit with positive work")
     bottleneck = max(per_unit, key=lambda u: (per_unit[u], u))
     return Bound(per_unit_us=per_unit, bound_us=per_unit[bottleneck], bottleneck=bottleneck)
 

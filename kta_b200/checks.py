@@ -48,24 +48,24 @@ def compare_output(got: np.ndarray, ref: np.ndarray, tol: dict[str, Any]) -> dic
     with np.errstate(invalid="ignore", over="ignore"):
         g = np.asarray(got).astype(np.float64)
         r = np.asarray(ref, dtype=np.float64)
-        both_nan = np.isnan(g) & np.isnan(r)
-        same_inf = np.isinf(g) & np.isinf(r) & (np.sign(g) == np.sign(r))
+        nan_on_both = np.isnan(g) & np.isnan(r)
+        inf_agrees = np.isinf(g) & np.isinf(r) & (np.sign(g) == np.sign(r))
         err = np.abs(g - r)
-        ok = (err <= float(tol["atol"]) + float(tol["rtol"]) * np.abs(r)) | both_nan | same_inf
+        ok = (err <= float(tol["atol"]) + float(tol["rtol"]) * np.abs(r)) | nan_on_both | inf_agrees
         finite = np.isfinite(r)
         diff = np.where(finite & np.isfinite(g), g - r, 0.0)
         ref_norm = float(np.linalg.norm(np.where(finite, r, 0.0)))
         dn = float(np.linalg.norm(diff))
         rel_l2 = dn / ref_norm if ref_norm > 0 else dn
-        bad_nonfinite = int(np.count_nonzero(~np.isfinite(g) & finite))
+        n_spurious = int(np.count_nonzero(~np.isfinite(g) & finite))
         return {
             "mismatches": int(np.count_nonzero(~ok)),
             "elements": int(g.size),
             "nan_count": int(np.count_nonzero(np.isnan(g) & ~np.isnan(r))),
-            "nonfinite_where_ref_finite": bad_nonfinite,
+            "nonfinite_where_ref_finite": n_spurious,
             "max_abs_err": float(np.max(np.where(finite & np.isfinite(g), err, 0.0),
                                         initial=0.0)),
-            "rel_l2": rel_l2 if bad_nonfinite == 0 else None,
+            "rel_l2": rel_l2 if n_spurious == 0 else None,
         }
 
 
@@ -76,10 +76,10 @@ def relative_to_library(tol: dict[str, Any]) -> bool:
 def library_verdict(stats: dict[str, Any], lib: dict[str, Any], tol: dict[str, Any],
                     level: str) -> tuple[bool, dict[str, Any]]:
     factor = float(tol.get(level, 2.0))
-    l2_floor = float(tol.get("rel_l2_floor", 1e-6))
-    abs_floor = float(tol.get("abs_floor", 1e-3))
-    l2_limit = max(factor * float(lib["rel_l2"] or 0.0), l2_floor)
-    abs_limit = max(factor * float(lib["max_abs_err"]), abs_floor)
+    rel_l2_min = float(tol.get("rel_l2_floor", 1e-6))
+    abs_min = float(tol.get("abs_floor", 1e-3))
+    l2_limit = max(factor * float(lib["rel_l2"] or 0.0), rel_l2_min)
+    abs_limit = max(factor * float(lib["max_abs_err"]), abs_min)
     ok = (stats["nonfinite_where_ref_finite"] == 0 and stats["rel_l2"] is not None
           and stats["rel_l2"] <= l2_limit and stats["max_abs_err"] <= abs_limit)
     return ok, {
