@@ -174,7 +174,8 @@ __device__ __forceinline__ Segment segment_at(const Work& w, long long t, long l
 // while the CTA still streams) or the eight compute warps (the CTA's last segment, when they
 // have nothing else to do). sync() orders the group's shared- and global-memory writes before
 // every member's later accesses; the compute warps' version waits on an mbarrier with the
-// library's bounded wait, so a member that gave up never leaves the others waiting.
+// library's bounded wait, so if one warp gave up earlier the others stop at the wait's limit
+// (and record it) instead of waiting for good.
 struct WarpGroup {
   static constexpr int THREADS = 32;
   static constexpr int COMBINE_NC = 4;  // pieces whose loads go out together
